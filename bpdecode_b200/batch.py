@@ -1,0 +1,324 @@
+"""Batched constraint state for continuous-batching serving.
+
+Drop-in for bpdecode's ``batch.py`` (``src/bpdecode/batch.py``):
+:class:`ConstraintBatch`, :class:`GrammarCache`, :class:`MaskCache` and the
+``FREE`` / ``BROKEN`` sentinels keep their signatures and semantics. What
+changes is underneath:
+
+* the per-step kernels index the device-resident state pool through the slot
+  tensor themselves, so ``apply_mask`` and ``commit`` are one launch each with
+  no gather / scatter copies of the states;
+* the slot tensor for a given ``seq_ids`` sequence is built once and reused
+  until the batch membership changes (the reference rebuilds and uploads it
+  from a Python list on every call, batch.py:171-174);
+* :meth:`ConstraintBatch.step_greedy` fuses mask + argmax + commit;
+* a batch may mix grammars (NEW): pass a list of :class:`FsaTensors` and
+  ``add(seq_id, grammar=i)``; their states are concatenated into one global
+  state space so a mixed batch is still one launch per step (the reference is
+  single-grammar per batch, batch.py:16-18).
+"""
+
+from __future__ import annotations
+
+from collections import OrderedDict, defaultdict
+from collections.abc import Hashable, Sequence
+
+import torch
+
+from . import _capi
+from .ops import (
+    FsaTensors,
+    _check_logits,
+    _require_cuda,
+    _stream,
+    _tokens,
+    apply_mask_,
+)
+
+FREE = -2  # slot holds no sequence
+BROKEN = -1  # a committed token left the grammar-valid path
+
+
+class MaskCache:
+    """LRU cache of allow-sets keyed by DFA state (batch.py:35-86).
+
+    Kept for API compatibility: with the packed allow rows resident on the
+    device, the uncached kernel path is already a per-state lookup, so the
+    cache no longer saves work -- it returns identical logits.
+    """
+
+    def __init__(self, fsa: FsaTensors, max_states: int = 512) -> None:
+        self._fsa = fsa
+        self._vocab = int(fsa.offsets.numel() - 1)
+        self._max = max_states
+        self._allowed: OrderedDict[int, torch.Tensor] = OrderedDict()
+
+    def _compute(self, state: int) -> torch.Tensor:
+        probe = torch.zeros(1, self._vocab, device=self._fsa.device)
+        st = torch.tensor([state], dtype=torch.int32, device=self._fsa.device)
+        apply_mask_(probe, self._fsa, st)
+        return (probe[0] == 0.0).nonzero(as_tuple=False).squeeze(1).to(torch.long)
+
+    def allowed_ids(self, state: int) -> torch.Tensor:
+        hit = self._allowed.get(state)
+        if hit is not None:
+            self._allowed.move_to_end(state)
+            return hit
+        ids = self._compute(state)
+        self._allowed[state] = ids
+        if len(self._allowed) > self._max:
+            self._allowed.popitem(last=False)
+        return ids
+
+    def __len__(self) -> int:
+        return len(self._allowed)
+
+    def apply(
+        self, states: torch.Tensor, logits: torch.Tensor, neg_inf: float = float("-inf")
+    ) -> torch.Tensor:
+        """In place: mask ``logits`` [n, vocab] given one state per row."""
+        by_state: dict[int, list[int]] = defaultdict(list)
+        for i, s in enumerate(states.tolist()):
+            by_state[s].append(i)
+        for state, rows in by_state.items():
+            allowed = self.allowed_ids(state).to(logits.device)
+            r = torch.tensor(rows, device=logits.device)
+            keep = logits.index_select(0, r).index_select(1, allowed)
+            logits[r] = neg_inf
+            logits[r.unsqueeze(1), allowed] = keep
+        return logits
+
+
+class GrammarCache:
+    """LRU cache of compiled grammars for one tokenizer / device (batch.py:89-115)."""
+
+    def __init__(self, vocab: object, device: torch.device | str = "cpu", max_size: int = 128,
+                 ) -> None:
+        self._vocab = vocab
+        self._device = torch.device(device)
+        self._max = max_size
+        self._cache: OrderedDict[str, FsaTensors] = OrderedDict()
+
+    def get(self, pattern: str) -> FsaTensors:
+        hit = self._cache.get(pattern)
+        if hit is not None:
+            self._cache.move_to_end(pattern)
+            return hit
+        fsa = FsaTensors.build(pattern, self._vocab).to(self._device)
+        self._cache[pattern] = fsa
+        if len(self._cache) > self._max:
+            self._cache.popitem(last=False)
+        return fsa
+
+    def __len__(self) -> int:
+        return len(self._cache)
+
+
+class _Tables:
+    """Device tables of the batch's grammars in one global state space."""
+
+    def __init__(self, grammars: list[FsaTensors]) -> None:
+        self.offsets: list[int] = []
+        total = 0
+        for g in grammars:
+            self.offsets.append(total)
+            total += g.num_states
+        self.num_states = total
+        self.vocab_size = grammars[0].vocab_size
+        if any(g.vocab_size != self.vocab_size for g in grammars):
+            raise ValueError("every grammar of a batch must share one vocabulary")
+        tables = [g.dense_tables() for g in grammars]
+        if len(grammars) == 1:
+            self.tok_next, self.allow_bits = tables[0]
+        else:
+            self.tok_next = torch.cat([
+                torch.where(tn >= 0, tn + off, tn) for (tn, _), off in zip(tables, self.offsets)])
+            self.allow_bits = torch.cat([b for _, b in tables])
+        self.starts = [g.start + off for g, off in zip(grammars, self.offsets)]
+        self.accepting = frozenset(
+            s + off for g, off in zip(grammars, self.offsets) for s in g.accepting)
+        las = [g.lookahead for g in grammars]
+        self.lookahead = None
+        if all(la is not None for la in las):
+            self.lookahead = las[0].contiguous() if len(las) == 1 else torch.cat(las)
+
+
+class ConstraintBatch:
+    """A fixed-capacity pool of grammar states (batch.py:118-226).
+
+    Slots are stable for a sequence's lifetime (``add`` -> ``evict``); the caller
+    passes an ordered list of sequence ids each step that lines up with its
+    logit rows. ``seq_ids`` of one call must be distinct.
+    """
+
+    _SLOT_CACHE = 8
+
+    def __init__(
+        self,
+        fsa: FsaTensors | Sequence[FsaTensors],
+        capacity: int,
+        device: torch.device | str | None = None,
+        mask_cache: bool | MaskCache = False,
+    ) -> None:
+        grammars = list(fsa) if isinstance(fsa, (list, tuple)) else [fsa]
+        if device is not None:
+            grammars = [g.to(device) for g in grammars]
+        self.grammars = grammars
+        self.fsa = grammars[0]
+        self.device = self.fsa.device
+        _require_cuda(self.fsa.trans, "ConstraintBatch tables")
+        self._t = _Tables(grammars)
+        self.capacity = capacity
+        self._state = torch.full((capacity,), FREE, dtype=torch.int32, device=self.device)
+        self._slot_of: dict[Hashable, int] = {}
+        self._grammar_of: dict[Hashable, int] = {}
+        self._free: list[int] = list(reversed(range(capacity)))
+        self._slot_cache: OrderedDict[tuple, torch.Tensor] = OrderedDict()
+        if mask_cache is True:
+            if len(grammars) != 1:
+                raise ValueError("mask_cache needs a single-grammar batch")
+            mask_cache = MaskCache(self.fsa)
+        self.cache: MaskCache | None = mask_cache or None
+
+    # --- lifecycle -------------------------------------------------------
+    def add(self, seq_id: Hashable, grammar: int = 0) -> int:
+        if seq_id in self._slot_of:
+            raise KeyError(f"sequence {seq_id!r} already in the batch")
+        if not self._free:
+            raise RuntimeError("ConstraintBatch is at capacity")
+        slot = self._free.pop()
+        self._slot_of[seq_id] = slot
+        self._grammar_of[seq_id] = grammar
+        self._state[slot] = self._t.starts[grammar]
+        self._slot_cache.clear()
+        return slot
+
+    def evict(self, seq_id: Hashable) -> None:
+        slot = self._slot_of.pop(seq_id)
+        self._grammar_of.pop(seq_id, None)
+        self._state[slot] = FREE
+        self._free.append(slot)
+        self._slot_cache.clear()
+
+    def reset(self, seq_id: Hashable) -> None:
+        self._state[self._slot_of[seq_id]] = self._t.starts[self._grammar_of[seq_id]]
+
+    def __len__(self) -> int:
+        return len(self._slot_of)
+
+    def __contains__(self, seq_id: Hashable) -> bool:
+        return seq_id in self._slot_of
+
+    # --- per-step ------------------------------------------------------
+    def _slots(self, seq_ids: Sequence[Hashable]) -> torch.Tensor:
+        key = seq_ids if isinstance(seq_ids, tuple) else tuple(seq_ids)
+        hit = self._slot_cache.get(key)
+        if hit is not None:
+            self._slot_cache.move_to_end(key)
+            return hit
+        slots = torch.tensor([self._slot_of[s] for s in key], dtype=torch.int64)
+        slots = slots.to(self.device, non_blocking=False)
+        self._slot_cache[key] = slots
+        if len(self._slot_cache) > self._SLOT_CACHE:
+            self._slot_cache.popitem(last=False)
+        return slots
+
+    def apply_mask(
+        self,
+        seq_ids: Sequence[Hashable],
+        logits: torch.Tensor,
+        neg_inf: float = float("-inf"),
+    ) -> torch.Tensor:
+        """In place: push every grammar-disallowed logit in ``logits``
+        ``[len(seq_ids), vocab]`` to ``neg_inf``, one row per ``seq_ids`` entry."""
+        slots = self._slots(seq_ids)
+        if self.cache is not None:
+            self.cache.apply(self._state[slots], logits, neg_inf)
+            return logits
+        t = self._t
+        B = int(slots.numel())
+        if int(logits.shape[0]) != B:
+            raise RuntimeError("bpdecode_b200: one logits row per seq_id")
+        code = _check_logits(logits, t.vocab_size)
+        L = _capi.lib()
+        L.check(L.bpd_dense_apply_mask(
+            logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
+            slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1], t.num_states,
+            float(neg_inf), _stream(logits)))
+        return logits
+
+    def apply_soft(
+        self,
+        seq_ids: Sequence[Hashable],
+        logits: torch.Tensor,
+        alpha: float = 1.0,
+    ) -> torch.Tensor:
+        """In place: add ``alpha * lookahead[state]`` per row (and mask, since
+        disallowed entries are ``-inf``); every grammar needs a lookahead table
+        (:meth:`FsaTensors.with_lookahead`)."""
+        t = self._t
+        if t.lookahead is None:
+            raise ValueError("fsa has no lookahead table; build with dense + with_lookahead")
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        code = _check_logits(logits, t.vocab_size)
+        L = _capi.lib()
+        L.check(L.bpd_soft_apply(
+            logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
+            slots.data_ptr(), t.lookahead.data_ptr(), t.num_states, float(alpha),
+            _stream(logits)))
+        return logits
+
+    def commit(self, seq_ids: Sequence[Hashable], tokens: torch.Tensor) -> torch.Tensor:
+        """Advance each named sequence by the token it sampled. Returns the new
+        state per sequence (``BROKEN`` if the token was off a valid path)."""
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        tk = _tokens(tokens, B, self.device)
+        nxt = torch.empty(B, dtype=torch.int32, device=self.device)
+        t = self._t
+        L = _capi.lib()
+        L.check(L.bpd_dense_advance(
+            self._state.data_ptr(), slots.data_ptr(), B, tk.data_ptr(),
+            int(tk.dtype == torch.int64), t.tok_next.data_ptr(), t.num_states, t.vocab_size,
+            nxt.data_ptr(), 1, _stream(nxt)))
+        return nxt
+
+    def step_greedy(
+        self,
+        seq_ids: Sequence[Hashable],
+        logits: torch.Tensor,
+        neg_inf: float = float("-inf"),
+        ctas_per_row: int = 0,
+    ) -> torch.Tensor:
+        """NEW: ``apply_mask`` + ``logits.argmax(-1)`` + ``commit`` in one
+        launch. Masks ``logits`` in place and returns the chosen tokens (int64,
+        torch.argmax semantics: first maximal index)."""
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        if int(logits.shape[0]) != B:
+            raise RuntimeError("bpdecode_b200: one logits row per seq_id")
+        t = self._t
+        code = _check_logits(logits, t.vocab_size)
+        tokens = torch.empty(B, dtype=torch.int64, device=self.device)
+        L = _capi.lib()
+        L.check(L.bpd_dense_step_greedy(
+            logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
+            slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1],
+            t.tok_next.data_ptr(), t.num_states, float(neg_inf), tokens.data_ptr(), None,
+            int(ctas_per_row), _stream(logits)))
+        return tokens
+
+    # --- queries ------------------------------------------------------
+    def state_of(self, seq_id: Hashable) -> int:
+        return int(self._state[self._slot_of[seq_id]])
+
+    def is_complete(self, seq_id: Hashable) -> bool:
+        """True when the string so far is a full match (EOS is allowed)."""
+        return self.state_of(seq_id) in self._t.accepting
+
+    def is_broken(self, seq_id: Hashable) -> bool:
+        return self.state_of(seq_id) == BROKEN
+
+
+__all__ = ["BROKEN", "FREE", "ConstraintBatch", "GrammarCache", "MaskCache"]

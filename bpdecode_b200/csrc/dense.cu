@@ -1,0 +1,511 @@
+// Dense regular path: per-state packed allow bits + the per-step mask, commit
+// and fused greedy step over bf16 / fp16 / fp32 logits.
+//
+// Reference semantics: ops.py:262-310 (dense branches of apply_mask_ and
+// advance_state), batch.py:176-215 (ConstraintBatch.apply_mask / commit) and
+// mask_cpu.cpp:51-90 (step / compute_mask bit layout).
+//
+// HBM design. A row-step must stream the row of logits once. The allow row of
+// a state is 1 bit per token (V/8 bytes, L2-resident: every row in one state
+// shares it), read once per 32 tokens by one lane and fanned out with a warp
+// shuffle. Each lane owns 16-byte vectors of logits; per vector:
+//   all tokens allowed    -> no load, no store (the fused step loads, for argmax)
+//   all tokens rejected   -> one 16-byte store of neg_inf, no load
+//   mixed                 -> load, blend, store
+// so a typical grammar state (almost everything rejected) moves about one
+// write of the row instead of a read plus a write.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <climits>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace bpd {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kVPT = 4;  // 16-byte vectors per lane per warp tile
+constexpr unsigned kAll = 0xFFFFFFFFu;
+
+template <typename T>
+constexpr int tile_elems() {
+  return 32 * kVPT * Dt<T>::kPerVec;
+}
+
+// ---------------------------------------------------------------------------
+// Table build (compile time).
+
+__device__ __forceinline__ int32_t dfa_step(const int32_t* __restrict__ trans, int32_t M,
+                                            const uint8_t* __restrict__ accept,
+                                            const uint8_t* __restrict__ live, int32_t dead,
+                                            const int32_t* __restrict__ offsets,
+                                            const int32_t* __restrict__ symbols, int32_t eos_id,
+                                            int32_t state, int32_t tok) {
+  if (tok == eos_id) return accept[state] ? state : -1;
+  int32_t cur = state;
+  const int32_t end = offsets[tok + 1];
+  for (int32_t i = offsets[tok]; i < end; ++i) {
+    const int32_t sym = symbols[i];
+    if (sym < 0 || sym >= M) return -1;
+    cur = trans[static_cast<int64_t>(cur) * M + sym];
+    if (cur == dead) return -1;
+  }
+  return live[cur] ? cur : -1;
+}
+
+__global__ void build_tok_next_kernel(const int32_t* __restrict__ trans, int32_t S, int32_t M,
+                                      const uint8_t* __restrict__ accept,
+                                      const uint8_t* __restrict__ live, int32_t dead,
+                                      const int32_t* __restrict__ offsets,
+                                      const int32_t* __restrict__ symbols, int32_t V,
+                                      int32_t eos_id, const int32_t* __restrict__ rows,
+                                      int32_t num_rows, int32_t* __restrict__ out) {
+  const int64_t total = static_cast<int64_t>(num_rows) * V;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int32_t r = static_cast<int32_t>(i / V);
+    const int32_t t = static_cast<int32_t>(i - static_cast<int64_t>(r) * V);
+    const int32_t s = rows ? rows[r] : r;
+    out[i] = (s < 0 || s >= S) ? -1
+                               : dfa_step(trans, M, accept, live, dead, offsets, symbols, eos_id,
+                                          s, t);
+  }
+}
+
+// One warp builds 32 consecutive words of one state's allow row: 32 coalesced
+// 128-byte loads of tok_next, one ballot each.
+__global__ void build_allow_bits_kernel(const int32_t* __restrict__ tok_next, int32_t S,
+                                        int32_t V, uint32_t* __restrict__ bits, int32_t wstride) {
+  const int32_t lane = threadIdx.x & 31;
+  const int64_t warp_id = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int32_t groups = (wstride + 31) / 32;
+  if (warp_id >= static_cast<int64_t>(S) * groups) return;
+  const int32_t s = static_cast<int32_t>(warp_id / groups);
+  const int32_t w0 = static_cast<int32_t>(warp_id - static_cast<int64_t>(s) * groups) * 32;
+  const int32_t* trow = tok_next + static_cast<int64_t>(s) * V;
+  uint32_t mine = 0;
+  for (int32_t j = 0; j < 32; ++j) {
+    const int32_t t = (w0 + j) * 32 + lane;
+    const bool ok = (w0 + j) < wstride && t < V && trow[t] != -1;
+    const uint32_t b = __ballot_sync(kAll, ok);
+    if (lane == j) mine = b;
+  }
+  if (w0 + lane < wstride) bits[static_cast<int64_t>(s) * wstride + w0 + lane] = mine;
+}
+
+// ---------------------------------------------------------------------------
+// Per-step streaming over one row segment.
+
+struct ArgState {
+  uint64_t best = 0;                 // packed (key, index) of the best allowed element
+  int32_t first_masked = INT_MAX;    // lowest rejected index seen by this thread
+};
+
+template <typename T, bool kArgmax>
+__device__ __forceinline__ void arg_update(ArgState& st, typename Dt<T>::Bits b, int32_t idx) {
+  if constexpr (kArgmax) {
+    const uint64_t p = pack_arg(order_key(Dt<T>::to_float(b)), idx);
+    st.best = p > st.best ? p : st.best;
+  }
+}
+
+template <bool kArgmax>
+__device__ __forceinline__ void arg_masked(ArgState& st, int32_t idx) {
+  if constexpr (kArgmax) st.first_masked = idx < st.first_masked ? idx : st.first_masked;
+}
+
+// Masks [c0, c1) of `row` (c0 a multiple of the warp tile, so allow words line
+// up) against allow row `brow` (nullptr = reject everything). With kArgmax the
+// thread also tracks the first maximal element of the masked row.
+template <typename T, bool kVec, bool kArgmax>
+__device__ __forceinline__ void mask_range(T* __restrict__ row, int32_t c0, int32_t c1,
+                                           const uint32_t* __restrict__ brow,
+                                           typename Dt<T>::Bits fill, ArgState& st) {
+  using Bits = typename Dt<T>::Bits;
+  constexpr int EPV = Dt<T>::kPerVec;
+  constexpr int TILE = tile_elems<T>();
+  constexpr int WPT = TILE / 32;  // allow words per warp tile
+  constexpr uint32_t FULL = (1u << EPV) - 1u;
+  const int32_t lane = threadIdx.x & 31;
+  const int32_t warp = threadIdx.x >> 5;
+  int32_t vend = c0;
+  if constexpr (kVec) {
+    const int32_t ntiles = c1 > c0 ? (c1 - c0) / TILE : 0;
+    vend = c0 + ntiles * TILE;
+    for (int32_t ti = warp; ti < ntiles; ti += kWarps) {
+      const int32_t tb = c0 + ti * TILE;
+      uint32_t w = 0;
+      if (brow != nullptr && lane < WPT) w = __ldg(brow + (tb >> 5) + lane);
+      uint32_t bits[kVPT];
+#pragma unroll
+      for (int j = 0; j < kVPT; ++j) {
+        const int v = lane + 32 * j;
+        const uint32_t word = __shfl_sync(kAll, w, (v * EPV) >> 5);
+        bits[j] = (word >> ((v * EPV) & 31)) & FULL;
+      }
+      uint4* base = reinterpret_cast<uint4*>(row + tb);
+      uint4 val[kVPT];
+#pragma unroll
+      for (int j = 0; j < kVPT; ++j) {
+        const bool need = kArgmax ? (bits[j] != 0u) : (bits[j] != 0u && bits[j] != FULL);
+        if (need) val[j] = __ldcs(base + lane + 32 * j);
+      }
+#pragma unroll
+      for (int j = 0; j < kVPT; ++j) {
+        const int32_t e0 = tb + (lane + 32 * j) * EPV;
+        if (bits[j] == FULL) {
+          if constexpr (kArgmax) {
+#pragma unroll
+            for (int i = 0; i < EPV; ++i) arg_update<T, true>(st, vec_get<T>(val[j], i), e0 + i);
+          }
+        } else if (bits[j] == 0u) {
+          __stcs(base + lane + 32 * j, vec_splat<T>(fill));
+          arg_masked<kArgmax>(st, e0);
+        } else {
+          __stcs(base + lane + 32 * j, vec_blend<T>(val[j], bits[j], fill));
+          if constexpr (kArgmax) {
+#pragma unroll
+            for (int i = 0; i < EPV; ++i) {
+              if ((bits[j] >> i) & 1u) {
+                arg_update<T, true>(st, vec_get<T>(val[j], i), e0 + i);
+              } else {
+                arg_masked<true>(st, e0 + i);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  Bits* rb = reinterpret_cast<Bits*>(row);
+  for (int32_t e = vend + static_cast<int32_t>(threadIdx.x); e < c1; e += kThreads) {
+    const bool allowed = brow != nullptr && ((__ldg(brow + (e >> 5)) >> (e & 31)) & 1u);
+    if (allowed) {
+      if constexpr (kArgmax) arg_update<T, true>(st, rb[e], e);
+    } else {
+      rb[e] = fill;
+      arg_masked<kArgmax>(st, e);
+    }
+  }
+}
+
+__device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__ pool,
+                                                     const int64_t* __restrict__ slots,
+                                                     int32_t row, const uint32_t* __restrict__ bits,
+                                                     int32_t wstride, int32_t S, int32_t* state,
+                                                     int64_t* slot_out) {
+  const int64_t slot = slots ? slots[row] : row;
+  const int32_t s = pool[slot];
+  *state = s;
+  if (slot_out) *slot_out = slot;
+  return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
+}
+
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kThreads)
+    dense_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V,
+                       const int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
+                       const uint32_t* __restrict__ bits, int32_t wstride, int32_t S,
+                       typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
+  const int32_t row = blockIdx.x / chunks_per_row;
+  const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
+  const int32_t c1 = min(V, c0 + chunk);
+  int32_t s;
+  const uint32_t* brow = state_row(pool, slots, row, bits, wstride, S, &s, nullptr);
+  ArgState st;
+  mask_range<T, kVec, false>(logits + row * row_stride, c0, c1, brow, fill, st);
+}
+
+// Fused greedy step. A thread-block cluster of `k` CTAs owns one row; every
+// CTA masks its slice and reduces its first-maximal element; the partials are
+// written into rank 0's shared memory (distributed shared memory), and after
+// one cluster barrier rank 0 commits the winning token.
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kThreads)
+    dense_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V,
+                      int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
+                      const uint32_t* __restrict__ bits, int32_t wstride,
+                      const int32_t* __restrict__ tok_next, int32_t S, typename Dt<T>::Bits fill,
+                      int32_t chunk, int64_t* __restrict__ token_out,
+                      int32_t* __restrict__ next_out) {
+  __shared__ uint64_t warp_best[kWarps];
+  __shared__ uint64_t cluster_best[8];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int32_t k = static_cast<int32_t>(cluster.num_blocks());
+  const int32_t rank = static_cast<int32_t>(cluster.block_rank());
+  const int32_t row = blockIdx.x / k;
+  const int32_t c0 = rank * chunk;
+  const int32_t c1 = min(V, c0 + chunk);
+  int32_t s;
+  int64_t slot;
+  const uint32_t* brow = state_row(pool, slots, row, bits, wstride, S, &s, &slot);
+
+  ArgState st;
+  mask_range<T, kVec, true>(logits + row * row_stride, c0, c1, brow, fill, st);
+
+  uint64_t mine = st.best;
+  if (st.first_masked != INT_MAX) {
+    const uint64_t m = pack_arg(order_key(Dt<T>::to_float(fill)), st.first_masked);
+    mine = m > mine ? m : mine;
+  }
+  mine = warp_max_u64(mine);
+  const int32_t lane = threadIdx.x & 31;
+  const int32_t warp = threadIdx.x >> 5;
+  if (lane == 0) warp_best[warp] = mine;
+  __syncthreads();
+  if (warp == 0) {
+    uint64_t q = lane < kWarps ? warp_best[lane] : 0;
+    q = warp_max_u64(q);
+    if (lane == 0) {
+      uint64_t* dst = cluster.map_shared_rank(cluster_best, 0);
+      dst[rank] = q;
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    uint64_t best = 0;
+    for (int32_t r = 0; r < k; ++r) best = cluster_best[r] > best ? cluster_best[r] : best;
+    const int32_t tok = unpack_idx(best);
+    const int32_t next =
+        (s >= 0 && s < S && tok >= 0 && tok < V) ? tok_next[static_cast<int64_t>(s) * V + tok] : -1;
+    pool[slot] = next;
+    token_out[row] = tok;
+    if (next_out) next_out[row] = next;
+  }
+}
+
+__global__ void dense_advance_kernel(int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
+                                     int32_t B, const void* __restrict__ tokens, int32_t tokens64,
+                                     const int32_t* __restrict__ tok_next, int32_t S, int32_t V,
+                                     int32_t* __restrict__ next_out, int32_t write_back) {
+  const int32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B) return;
+  const int64_t slot = slots ? slots[i] : i;
+  const int32_t s = pool[slot];
+  const int64_t t = tokens64 ? static_cast<const int64_t*>(tokens)[i]
+                             : static_cast<int64_t>(static_cast<const int32_t*>(tokens)[i]);
+  const int32_t n = (s < 0 || s >= S || t < 0 || t >= V)
+                        ? -1
+                        : tok_next[static_cast<int64_t>(s) * V + t];
+  if (next_out) next_out[i] = n;
+  if (write_back) pool[slot] = n;
+}
+
+__global__ void dense_mask_bits_kernel(const int32_t* __restrict__ pool,
+                                       const int64_t* __restrict__ slots, int32_t B,
+                                       const uint32_t* __restrict__ bits, int32_t wstride,
+                                       int32_t S, int32_t W, uint32_t* __restrict__ out) {
+  const int32_t row = blockIdx.y;
+  int32_t s;
+  const uint32_t* brow = state_row(pool, slots, row, bits, wstride, S, &s, nullptr);
+  for (int32_t w = blockIdx.x * blockDim.x + threadIdx.x; w < W; w += gridDim.x * blockDim.x)
+    out[static_cast<int64_t>(row) * W + w] = brow ? __ldg(brow + w) : 0u;
+}
+
+// ---------------------------------------------------------------------------
+
+int esize(int32_t dtype) { return dtype == BPD_F32 ? 4 : 2; }
+
+bool dtype_ok(int32_t dtype) { return dtype == BPD_F32 || dtype == BPD_BF16 || dtype == BPD_F16; }
+
+template <typename T>
+bpd_status launch_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
+                        const int32_t* pool, const int64_t* slots, const uint32_t* bits,
+                        int32_t wstride, int32_t S, float neg_inf, cudaStream_t st) {
+  constexpr int TILE = tile_elems<T>();
+  const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+  // ~2 warp tiles per warp per CTA: fine-grained enough to balance rows of
+  // different masks across 148 SMs.
+  const int32_t chunk = TILE * kWarps * 2;
+  const int32_t chunks = (V + chunk - 1) / chunk;
+  const int64_t grid = static_cast<int64_t>(batch) * chunks;
+  BPD_REQUIRE(grid < INT_MAX, "batch too large");
+  const auto fill = Dt<T>::from_float_host(neg_inf);
+  T* lg = static_cast<T*>(logits);
+  if (vec) {
+    dense_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+        lg, row_stride, V, pool, slots, bits, wstride, S, fill, chunk, chunks);
+  } else {
+    dense_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+        lg, row_stride, V, pool, slots, bits, wstride, S, fill, chunk, chunks);
+  }
+  return check_launch("dense_apply_kernel");
+}
+
+int32_t auto_ctas_per_row(int32_t batch) {
+  // aim for >= ~6 resident CTAs per SM across the 148 SMs
+  const int32_t want = (148 * 6 + batch - 1) / batch;
+  int32_t k = 1;
+  while (k < want && k < 8) k <<= 1;
+  return k;
+}
+
+template <typename T>
+bpd_status launch_step(void* logits, int64_t row_stride, int32_t batch, int32_t V, int32_t* pool,
+                       const int64_t* slots, const uint32_t* bits, int32_t wstride,
+                       const int32_t* tok_next, int32_t S, float neg_inf, int64_t* token_out,
+                       int32_t* next_out, int32_t k, cudaStream_t st) {
+  constexpr int TILE = tile_elems<T>();
+  const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+  const int32_t per = (V + k - 1) / k;
+  const int32_t chunk = ((per + TILE - 1) / TILE) * TILE;
+  const int64_t grid = static_cast<int64_t>(batch) * k;
+  BPD_REQUIRE(grid < INT_MAX, "batch too large");
+  const auto fill = Dt<T>::from_float_host(neg_inf);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(k);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  T* lg = static_cast<T*>(logits);
+  cudaError_t e;
+  if (vec) {
+    e = cudaLaunchKernelEx(&cfg, dense_step_kernel<T, true>, lg, row_stride, V, pool, slots, bits,
+                           wstride, tok_next, S, fill, chunk, token_out, next_out);
+  } else {
+    e = cudaLaunchKernelEx(&cfg, dense_step_kernel<T, false>, lg, row_stride, V, pool, slots, bits,
+                           wstride, tok_next, S, fill, chunk, token_out, next_out);
+  }
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "dense_step_kernel: %s", cudaGetErrorString(e));
+  return check_launch("dense_step_kernel");
+}
+
+}  // namespace
+}  // namespace bpd
+
+using namespace bpd;
+
+extern "C" bpd_status bpd_dense_build_tok_next(
+    const int32_t* trans, int32_t num_states, int32_t num_symbols, const uint8_t* accept,
+    const uint8_t* live, int32_t dead, const int32_t* tok_offsets, const int32_t* tok_symbols,
+    int32_t vocab_size, int32_t eos_id, const int32_t* rows, int32_t num_rows,
+    int32_t* tok_next_out, void* stream) {
+  BPD_REQUIRE(trans && accept && live && tok_offsets && tok_symbols && tok_next_out,
+              "bpd_dense_build_tok_next: null pointer");
+  BPD_REQUIRE(num_states > 0 && num_symbols > 0 && vocab_size > 0 && num_rows >= 0,
+              "bpd_dense_build_tok_next: bad sizes");
+  if (num_rows == 0) return BPD_OK;
+  const int64_t total = static_cast<int64_t>(num_rows) * vocab_size;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 32);
+  build_tok_next_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+      trans, num_states, num_symbols, accept, live, dead, tok_offsets, tok_symbols, vocab_size,
+      eos_id, rows, num_rows, tok_next_out);
+  return check_launch("build_tok_next_kernel");
+}
+
+extern "C" bpd_status bpd_dense_build_allow_bits(const int32_t* tok_next, int32_t num_states,
+                                                 int32_t vocab_size, uint32_t* bits_out,
+                                                 int32_t words_stride, void* stream) {
+  BPD_REQUIRE(tok_next && bits_out, "bpd_dense_build_allow_bits: null pointer");
+  BPD_REQUIRE(num_states > 0 && vocab_size > 0, "bpd_dense_build_allow_bits: bad sizes");
+  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32 && words_stride % 4 == 0,
+              "bpd_dense_build_allow_bits: words_stride must be >= ceil(vocab/32) and a multiple of 4");
+  const int64_t warps = static_cast<int64_t>(num_states) * ((words_stride + 31) / 32);
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  build_allow_bits_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+      tok_next, num_states, vocab_size, bits_out, words_stride);
+  return check_launch("build_allow_bits_kernel");
+}
+
+extern "C" bpd_status bpd_dense_apply_mask(void* logits, int32_t dtype, int64_t row_stride,
+                                           int32_t batch, int32_t vocab_size,
+                                           const int32_t* state_pool, const int64_t* slots,
+                                           const uint32_t* allow_bits, int32_t words_stride,
+                                           int32_t num_states, float neg_inf, void* stream) {
+  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_dense_apply_mask: bad sizes");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(logits && state_pool && allow_bits, "bpd_dense_apply_mask: null pointer");
+  BPD_REQUIRE(dtype_ok(dtype), "bpd_dense_apply_mask: unsupported logits dtype %d", dtype);
+  BPD_REQUIRE(row_stride >= vocab_size, "bpd_dense_apply_mask: row_stride < vocab");
+  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32, "bpd_dense_apply_mask: words_stride too small");
+  (void)esize;
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case BPD_F32:
+      return launch_apply<float>(logits, row_stride, batch, vocab_size, state_pool, slots,
+                                 allow_bits, words_stride, num_states, neg_inf, st);
+    case BPD_BF16:
+      return launch_apply<__nv_bfloat16>(logits, row_stride, batch, vocab_size, state_pool, slots,
+                                         allow_bits, words_stride, num_states, neg_inf, st);
+    default:
+      return launch_apply<__half>(logits, row_stride, batch, vocab_size, state_pool, slots,
+                                  allow_bits, words_stride, num_states, neg_inf, st);
+  }
+}
+
+extern "C" bpd_status bpd_dense_advance(int32_t* state_pool, const int64_t* slots, int32_t batch,
+                                        const void* tokens, int32_t tokens_int64,
+                                        const int32_t* tok_next, int32_t num_states,
+                                        int32_t vocab_size, int32_t* next_out, int32_t write_back,
+                                        void* stream) {
+  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_dense_advance: bad sizes");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(state_pool && tokens && tok_next, "bpd_dense_advance: null pointer");
+  const int32_t blocks = (batch + 255) / 256;
+  dense_advance_kernel<<<blocks, 256, 0, as_stream(stream)>>>(
+      state_pool, slots, batch, tokens, tokens_int64, tok_next, num_states, vocab_size, next_out,
+      write_back);
+  return check_launch("dense_advance_kernel");
+}
+
+extern "C" bpd_status bpd_dense_mask_bits(const int32_t* state_pool, const int64_t* slots,
+                                          int32_t batch, const uint32_t* allow_bits,
+                                          int32_t words_stride, int32_t num_states,
+                                          int32_t vocab_size, uint32_t* out_bits, void* stream) {
+  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_dense_mask_bits: bad sizes");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(state_pool && allow_bits && out_bits, "bpd_dense_mask_bits: null pointer");
+  BPD_REQUIRE(batch <= 65535, "bpd_dense_mask_bits: batch > 65535");
+  const int32_t W = (vocab_size + 31) / 32;
+  dim3 grid((W + 255) / 256, batch);
+  dense_mask_bits_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+      state_pool, slots, batch, allow_bits, words_stride, num_states, W, out_bits);
+  return check_launch("dense_mask_bits_kernel");
+}
+
+extern "C" bpd_status bpd_dense_step_greedy(void* logits, int32_t dtype, int64_t row_stride,
+                                            int32_t batch, int32_t vocab_size, int32_t* state_pool,
+                                            const int64_t* slots, const uint32_t* allow_bits,
+                                            int32_t words_stride, const int32_t* tok_next,
+                                            int32_t num_states, float neg_inf, int64_t* token_out,
+                                            int32_t* next_out, int32_t ctas_per_row,
+                                            void* stream) {
+  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_dense_step_greedy: bad sizes");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(logits && state_pool && allow_bits && tok_next && token_out,
+              "bpd_dense_step_greedy: null pointer");
+  BPD_REQUIRE(dtype_ok(dtype), "bpd_dense_step_greedy: unsupported logits dtype %d", dtype);
+  BPD_REQUIRE(row_stride >= vocab_size, "bpd_dense_step_greedy: row_stride < vocab");
+  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
+              "bpd_dense_step_greedy: words_stride too small");
+  BPD_REQUIRE(ctas_per_row == 0 || ctas_per_row == 1 || ctas_per_row == 2 || ctas_per_row == 4 ||
+                  ctas_per_row == 8,
+              "bpd_dense_step_greedy: ctas_per_row must be 0, 1, 2, 4 or 8");
+  const int32_t k = ctas_per_row ? ctas_per_row : auto_ctas_per_row(batch);
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case BPD_F32:
+      return launch_step<float>(logits, row_stride, batch, vocab_size, state_pool, slots,
+                                allow_bits, words_stride, tok_next, num_states, neg_inf,
+                                token_out, next_out, k, st);
+    case BPD_BF16:
+      return launch_step<__nv_bfloat16>(logits, row_stride, batch, vocab_size, state_pool, slots,
+                                        allow_bits, words_stride, tok_next, num_states, neg_inf,
+                                        token_out, next_out, k, st);
+    default:
+      return launch_step<__half>(logits, row_stride, batch, vocab_size, state_pool, slots,
+                                 allow_bits, words_stride, tok_next, num_states, neg_inf,
+                                 token_out, next_out, k, st);
+  }
+}

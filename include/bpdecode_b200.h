@@ -1,0 +1,228 @@
+/*
+ * bpdecode_b200 -- C ABI of the B200 (sm_100a) constrained-decoding step.
+ *
+ * This is the drop-in boundary that replaces bpdecode's torch-op binding
+ * (bindings/torch_ops.cpp) and the pure-torch dense path of ops.py. Every
+ * entry point takes plain device pointers and sizes -- no torch types -- and
+ * enqueues its kernels on `stream` (a cudaStream_t, NULL = legacy default)
+ * without synchronising, exactly like the reference ops, which launch on
+ * torch's current stream (bindings/torch_ops.cpp:36-42).
+ *
+ * Errors: every function returns a bpd_status. BPD_OK (0) means the work was
+ * enqueued; anything else means nothing was enqueued and bpd_last_error()
+ * returns a message for the calling thread. The Python layer turns a non-zero
+ * status into RuntimeError, which is what TORCH_CHECK raises in the reference
+ * (bindings/torch_ops.cpp:47-51,115-120,301-305,335-339).
+ *
+ * Layouts (identical to the reference unless marked NEW):
+ *   states / state pool  int32, -1 = BROKEN, -2 = FREE (batch.py:31-32)
+ *   tok_next             int32 [num_states, vocab] row-major, -1 = reject,
+ *                        EOS column = s if s accepts else -1 (ops.py:143-197)
+ *   allow bits (NEW)     uint32 [num_states, words_stride], bit t of word t>>5
+ *                        set iff tok_next[s,t] != -1 (LSB first, as the
+ *                        compute_mask op, mask.hpp:528-531)
+ *   PDA config-set       int32 [266] = num_configs, saturated, depth[8],
+ *                        stack[8][32] (pda.hpp:82-91)
+ *   logits               dtype BPD_F32 / BPD_BF16 / BPD_F16, rows `row_stride`
+ *                        elements apart, columns contiguous
+ *   slots                optional int64 [batch]: row b reads/writes
+ *                        pool[slots[b]]; NULL means row b uses pool[b]
+ */
+#ifndef BPDECODE_B200_H_
+#define BPDECODE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t bpd_status;
+#define BPD_OK 0
+#define BPD_ERR_INVALID 1   /* bad argument: null pointer, size, dtype, alignment */
+#define BPD_ERR_CUDA 2      /* a CUDA runtime call or launch failed */
+#define BPD_ERR_CAPACITY 3  /* a size exceeds a documented maximum */
+
+#define BPD_F32 0
+#define BPD_BF16 1
+#define BPD_F16 2
+
+#define BPD_PDA_MAX_CONFIGS 8
+#define BPD_PDA_MAX_DEPTH 32
+#define BPD_PDA_CONFIG_INTS (2 + BPD_PDA_MAX_CONFIGS + BPD_PDA_MAX_CONFIGS * BPD_PDA_MAX_DEPTH)
+
+/* Library version string. */
+const char* bpd_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* bpd_last_error(void);
+
+/* --------------------------------------------------------------------------
+ * Dense regular path (regex / non-recursive JSON Schema compiled to a DFA)
+ * ------------------------------------------------------------------------ */
+
+/* Dense next-state table from the byte-class DFA: out[r, t] = step(rows[r], t)
+ * for every token t (rows == NULL: r = 0..num_rows-1 are the states).
+ * Replaces ops.py:143-197 (build_token_transitions); semantics of
+ * mask_cpu.cpp:51-67 (step), EOS column as ops.py:190-196. */
+bpd_status bpd_dense_build_tok_next(
+    const int32_t* trans, int32_t num_states, int32_t num_symbols,
+    const uint8_t* accept, const uint8_t* live, int32_t dead,
+    const int32_t* tok_offsets, const int32_t* tok_symbols, int32_t vocab_size,
+    int32_t eos_id, const int32_t* rows, int32_t num_rows, int32_t* tok_next_out,
+    void* stream);
+
+/* NEW: packed allow bits of every tok_next row (bit = tok_next != -1).
+ * words_stride >= ceil(vocab/32), a multiple of 4; padding words are zeroed. */
+bpd_status bpd_dense_build_allow_bits(
+    const int32_t* tok_next, int32_t num_states, int32_t vocab_size,
+    uint32_t* bits_out, int32_t words_stride, void* stream);
+
+/* In place: logits[b, t] = neg_inf where state < 0 (BROKEN / FREE), state is
+ * out of range, or bit t of the state's allow row is clear. Replaces the dense
+ * branch of apply_mask_ (ops.py:271-276) and the apply_mask_ op
+ * (bindings/torch_ops.cpp:109-152). neg_inf is rounded to the logits dtype
+ * (round to nearest even, as masked_fill_). */
+bpd_status bpd_dense_apply_mask(
+    void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
+    int32_t vocab_size, const int32_t* state_pool, const int64_t* slots,
+    const uint32_t* allow_bits, int32_t words_stride, int32_t num_states,
+    float neg_inf, void* stream);
+
+/* Commit: next[b] = state < 0 ? -1 : tok_next[state, token[b]] (token out of
+ * [0, vocab) -> -1); written to next_out (may be NULL) and, if write_back,
+ * into state_pool[slots[b]]. tokens are int32 or int64 (tokens_int64 != 0).
+ * Replaces the dense branch of advance_state (ops.py:301-306) and
+ * ConstraintBatch.commit's gather/scatter (batch.py:206-215). */
+bpd_status bpd_dense_advance(
+    int32_t* state_pool, const int64_t* slots, int32_t batch, const void* tokens,
+    int32_t tokens_int64, const int32_t* tok_next, int32_t num_states,
+    int32_t vocab_size, int32_t* next_out, int32_t write_back, void* stream);
+
+/* Packed allow bits per row, int32 [batch, ceil(vocab/32)] (the compute_mask
+ * op, ops.py:284-292 / bindings/torch_ops.cpp:154-189); zero rows for
+ * state < 0. */
+bpd_status bpd_dense_mask_bits(
+    const int32_t* state_pool, const int64_t* slots, int32_t batch,
+    const uint32_t* allow_bits, int32_t words_stride, int32_t num_states,
+    int32_t vocab_size, uint32_t* out_bits, void* stream);
+
+/* NEW fused greedy step: apply_mask (as bpd_dense_apply_mask) + argmax of the
+ * masked row (first maximal index, NaN counts as maximal, like torch.argmax)
+ * + commit of that token (as bpd_dense_advance with write_back = 1).
+ * token_out int64 [batch]; next_out int32 [batch] may be NULL.
+ * ctas_per_row (0 = automatic, else 1, 2, 4 or 8) CTAs, one thread-block
+ * cluster, share one row and reduce the argmax through distributed shared
+ * memory. */
+bpd_status bpd_dense_step_greedy(
+    void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
+    int32_t vocab_size, int32_t* state_pool, const int64_t* slots,
+    const uint32_t* allow_bits, int32_t words_stride, const int32_t* tok_next,
+    int32_t num_states, float neg_inf, int64_t* token_out, int32_t* next_out,
+    int32_t ctas_per_row, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Soft lookahead (k-step backward sum-product bias)
+ * ------------------------------------------------------------------------ */
+
+/* Lookahead table out[s, t] = logZ_{k-1}(tok_next[s, t]) in fp32, -inf where
+ * tok_next = -1, EOS column 0 / -inf by accept. Replaces ops.py:200-236.
+ * workspace: at least bpd_soft_workspace_bytes(num_states) bytes. */
+size_t bpd_soft_workspace_bytes(int32_t num_states);
+bpd_status bpd_soft_build_lookahead(
+    const int32_t* tok_next, int32_t num_states, int32_t vocab_size,
+    const uint8_t* accept, const uint8_t* live, int32_t eos_id, int32_t k,
+    float* out, void* workspace, void* stream);
+
+/* In place: logits += alpha * bias on entries where bias is finite (skipped
+ * when alpha == 0), then logits = -inf where bias is -inf; bias =
+ * lookahead[state], all -inf for state < 0. Replaces ops.py:239-259. */
+bpd_status bpd_soft_apply(
+    void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
+    int32_t vocab_size, const int32_t* state_pool, const int64_t* slots,
+    const float* lookahead, int32_t num_states, float alpha, void* stream);
+
+/* --------------------------------------------------------------------------
+ * Pushdown automaton (context-free grammars)
+ * ------------------------------------------------------------------------ */
+
+/* The flattened grammar + token bytes (grammar/device.py:33-76): plain
+ * device pointers, as the reference's PdaTableView (pda_cuda.cu:22-33). */
+typedef struct bpd_pda_grammar {
+  int32_t num_states;
+  int32_t num_edges;
+  int32_t root_start;
+  int32_t root_accept;
+  const uint8_t* accept;        /* [num_states] */
+  const uint8_t* live;          /* [num_states] */
+  const int32_t* edge_offsets;  /* [num_states + 1] */
+  const int32_t* edge_kind;     /* [num_edges] 0 eps, 1 byte range, 2 call */
+  const int32_t* edge_lo;       /* [num_edges] */
+  const int32_t* edge_hi;       /* [num_edges] */
+  const int32_t* edge_dst;      /* [num_edges] */
+  const int32_t* edge_callee;   /* [num_edges] */
+  int32_t vocab_size;
+  int32_t eos_id;               /* -1: none */
+  const int32_t* tok_offsets;   /* [vocab_size + 1] */
+  const uint8_t* tok_bytes;     /* [tok_offsets[vocab_size]] */
+} bpd_pda_grammar;
+
+/* Initial config-set (pda.hpp:200-207) into config_out[266], on the device.
+ * Replaces the host pda_init op (bindings/torch_ops.cpp:307-324). */
+bpd_status bpd_pda_init(const bpd_pda_grammar* g, int32_t* config_out, void* stream);
+
+/* Mask-memo table in caller-owned device memory (NEW; the per-config mask memo
+ * held in HBM). bpd_pda_memo_bytes gives the size for `capacity` entries;
+ * bpd_pda_memo_reset clears it (call once after allocating, and to drop every
+ * cached mask). capacity must be a power of two. */
+size_t bpd_pda_memo_bytes(int32_t capacity, int32_t vocab_size);
+bpd_status bpd_pda_memo_reset(void* memo, int32_t capacity, int32_t vocab_size,
+                              void* stream);
+
+/* Per-call scratch of bpd_pda_apply_mask / bpd_pda_mask_bits for `batch` rows. */
+size_t bpd_pda_workspace_bytes(int32_t batch, int32_t vocab_size);
+
+/* Packed allow bits per row, int32 [batch, ceil(vocab/32)], of config-set
+ * pool[slots[b]] (compute_mask_pda_batch, pda_cpu.cpp:7-21). memo may be NULL
+ * (no caching). Rows whose broken flag is set (broken may be NULL) get zeros. */
+bpd_status bpd_pda_mask_bits(
+    const bpd_pda_grammar* g, const int32_t* config_pool, const int64_t* slots,
+    const uint8_t* broken, int32_t batch, void* memo, int32_t memo_capacity,
+    void* workspace, uint32_t* out_bits, void* stream);
+
+/* In place: logits[b, t] = neg_inf where token t is rejected from config-set
+ * pool[slots[b]] (pda_try_token, pda.hpp:248-258; EOS allowed iff complete)
+ * and on every column of rows whose broken flag is set. Replaces the
+ * pda_apply_mask_ op (bindings/torch_ops.cpp:326-376) plus the broken-row fill
+ * of CFGConstraintBatch.apply_mask (grammar/device.py:252-266), without the
+ * host sync. Any logits dtype. */
+bpd_status bpd_pda_apply_mask(
+    const bpd_pda_grammar* g, void* logits, int32_t dtype, int64_t row_stride,
+    const int32_t* config_pool, const int64_t* slots, const uint8_t* broken,
+    int32_t batch, void* memo, int32_t memo_capacity, void* workspace,
+    float neg_inf, void* stream);
+
+/* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64).
+ * ok_out[b] (uint8, may be NULL) = 1 if the token was accepted; a rejected
+ * token leaves the config-set unchanged; EOS sets ok = complete and never
+ * changes it (pda_cpu.cpp:35-54). If broken != NULL: broken[slot] |= !ok, and
+ * status_out[b] (int32, may be NULL) = broken[slot] ? -1 : 1
+ * (grammar/device.py:268-283). Replaces the pda_advance_state op
+ * (bindings/torch_ops.cpp:378-425). */
+bpd_status bpd_pda_advance(
+    const bpd_pda_grammar* g, int32_t* config_pool, const int64_t* slots,
+    int32_t batch, const void* tokens, int32_t tokens_int64, uint8_t* ok_out,
+    uint8_t* broken, int32_t* status_out, void* stream);
+
+/* complete_out[b] (uint8) = pda_is_complete(pool[slots[b]]) && !broken
+ * (pda.hpp:238-244; CFGConstraintBatch.is_complete, grammar/device.py:286-297). */
+bpd_status bpd_pda_is_complete(
+    const bpd_pda_grammar* g, const int32_t* config_pool, const int64_t* slots,
+    const uint8_t* broken, int32_t batch, uint8_t* complete_out, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* BPDECODE_B200_H_ */
