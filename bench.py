@@ -1,0 +1,458 @@
+"""Benchmark of the constrained-decoding step (row-steps/s + HBM roofline).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the serving-scale dense configuration): V = 128,256 synthetic
+tokens, 1024 rows per GPU, each row constrained by one of 8 regexes (IPv4,
+date, e-mail, signed float, hex colour, UUID, name, phone) chosen from the
+seed, bf16 logits ~ N(0, 2), greedy (argmax) commit. A step is mask + apply +
+argmax + commit of every row: one fused launch per step
+(ConstraintBatch.step_greedy). Rows are sharded by request: every rank owns
+1024 rows and no collective runs on the hot path (weak scaling).
+
+Prints one JSON line (rank 0). Under torchrun each rank runs on LOCAL_RANK;
+timing is the max over ranks of CUDA-event time.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+V = 128_256
+ROWS_PER_GPU = 1024
+SIGMA = 2.0
+METRIC = "constrained row-steps/sec (mask+apply+commit)"
+UNIT = "row-steps/s"
+# Algorithmic bytes of one row-step (bf16 logits, V = 128,256): logits read +
+# write 2*V*2, packed allow row 4*ceil(V/32), state/token/tok_next gather 16.
+E = 2
+ALGO_BYTES_PER_ROW_STEP = 2 * V * E + 4 * ((V + 31) // 32) + 16
+
+
+def _dist() -> tuple[int, int, int]:
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def _peaks() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def _profile_traffic() -> float | None:
+    """DRAM bytes per launch of the fused step kernel from the committed ncu
+    summary (a line `traffic_bytes_per_launch: N`), if present."""
+    path = os.path.join(ROOT, "profiles", "dense_step_config2.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    HW = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+          "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, index: int, period_s: float = 0.002) -> None:
+        self.index, self.period = index, period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz: int | None = None
+        self._stop = threading.Event()
+        self._thread: threading.Thread | None = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = int(pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self._nv = None
+
+    def _run(self) -> None:
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                clk = int(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+                self.samples.append((clk, rs))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self) -> ClockSampler:
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"],
+                    "samples": 0}
+        reasons = set()
+        for _, r in self.samples:
+            for name, bit in self.HW.items():
+                if r & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(self.samples)}
+
+
+def build_workload(rank: int, device: torch.device):
+    from bpdecode_b200 import tables
+    from bpdecode_b200.batch import ConstraintBatch
+    from bpdecode_b200.ops import FsaTensors
+    from bpdecode_b200.workloads import DENSE_PATTERNS, row_patterns, vocab_large
+
+    vocab = vocab_large(V)
+    fsas = [FsaTensors.from_arrays(tables.load_dfa(n), vocab).to(device)
+            for n, _ in DENSE_PATTERNS]
+    return vocab, fsas, row_patterns(ROWS_PER_GPU, seed=rank)
+
+
+def make_batch(fsas, pats):
+    from bpdecode_b200.batch import ConstraintBatch
+
+    batch = ConstraintBatch(fsas, capacity=ROWS_PER_GPU)
+    for i in range(ROWS_PER_GPU):
+        batch.add(i, grammar=pats[i])
+    return batch
+
+
+def gen_logits(rank: int, step: int, device: torch.device, out: torch.Tensor | None = None):
+    g = torch.Generator(device=device).manual_seed(rank * 1_000_003 + step)
+    x = torch.randn(ROWS_PER_GPU, V, generator=g, device=device) * SIGMA
+    if out is None:
+        return x.to(torch.bfloat16)
+    out.copy_(x)
+    return out
+
+
+def cpu_baseline(tok_next_cpu: torch.Tensor, starts: list[int], pats: list[int],
+                 rows: int, steps: int) -> dict:
+    """The reference's own dense torch step on host cores (all torch threads)."""
+    from oracle import torch_port
+
+    state = torch.tensor([starts[p] for p in pats[:rows]], dtype=torch.int32)
+    slots = torch.arange(rows)
+    g = torch.Generator().manual_seed(12345)
+    samples = [(torch.randn(rows, V, generator=g) * SIGMA).to(torch.bfloat16)
+               for _ in range(min(steps, 4))]
+    torch_port.step(samples[0], tok_next_cpu, state.clone(), slots)  # warm
+    t0 = time.perf_counter()
+    for i in range(steps):
+        torch_port.step(samples[i % len(samples)], tok_next_cpu, state, slots)
+    dt = time.perf_counter() - t0
+    return {"value": rows * steps / dt, "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{rows} of the {ROWS_PER_GPU} rows x {steps} steps, bf16, V={V}, "
+                      "torch CPU restatement of ops.py:271-276/301-306 + argmax "
+                      f"({dt:.1f} s)"}
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    """--impl reference: the reference's CPU implementation of the step, timed
+    on host cores on this workload; rank 0 only."""
+    rank, world, _ = _dist()
+    if rank != 0:
+        return
+    from bpdecode_b200 import tables
+    from bpdecode_b200.workloads import DENSE_PATTERNS, row_patterns, vocab_large
+    from oracle.oracle import Oracle, dfa_with_vocab
+
+    vocab = vocab_large(V)
+    orc = Oracle()
+    tns, starts, off = [], [], 0
+    for n, _ in DENSE_PATTERNS:
+        d = tables.load_dfa(n)
+        o, s = dfa_with_vocab(d, vocab.token_bytes)
+        tn = torch.from_numpy(orc.build_tok_next(d, o, s, vocab.eos_id))
+        tns.append(torch.where(tn >= 0, tn + off, tn))
+        starts.append(d["start"] + off)
+        off += tn.shape[0]
+    tok_next = torch.cat(tns)
+    pats = row_patterns(ROWS_PER_GPU, seed=0)
+    rows = 32
+    state = torch.tensor([starts[p] for p in pats[:rows]], dtype=torch.int32)
+    slots = torch.arange(rows)
+    g = torch.Generator().manual_seed(12345)
+    pool = [(torch.randn(rows, V, generator=g) * SIGMA).to(torch.bfloat16) for _ in range(4)]
+    from oracle import torch_port
+
+    for i in range(args.warmup):
+        torch_port.step(pool[i % 4], tok_next, state, slots)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        torch_port.step(pool[i % 4], tok_next, state, slots)
+    dt = time.perf_counter() - t0
+    value = rows * args.steps / dt
+    sample = (f"{rows} rows per step of the {ROWS_PER_GPU}-row workload, bf16, V={V}; torch "
+              "CPU restatement of bpdecode's dense step (ops.py:271-276/301-306 + argmax); "
+              "bpdecode's dense path is torch, not compiled code")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * dt / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": _config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config(world: int) -> dict:
+    return {
+        "workload": "dense regex step at serving scale: 8 regexes mixed per batch, "
+                    f"V={V}, {ROWS_PER_GPU} rows per GPU, bf16 logits N(0,{SIGMA:g}), argmax commit",
+        "vocab": V, "rows_per_gpu": ROWS_PER_GPU, "global_batch": ROWS_PER_GPU * world,
+        "parallelism": f"dp{world} (rows sharded by request, no collective)",
+        "l2": "inputs larger than L2: every step reads a fresh 262 MB logits buffer",
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ring", type=int, default=128, help="distinct logits buffers")
+    ap.add_argument("--e2e-steps", type=int, default=24)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    rank, world, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+
+    vocab, fsas, pats = build_workload(rank, device)
+    batch = make_batch(fsas, pats)
+    ids = list(range(ROWS_PER_GPU))
+
+    ring = max(1, min(args.ring, args.steps + args.warmup))
+    bufs = [gen_logits(rank, i, device) for i in range(ring)]
+    torch.cuda.synchronize()
+
+    def barrier() -> None:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    # warm-up
+    for i in range(args.warmup):
+        batch.step_greedy(ids, bufs[i % ring])
+    torch.cuda.synchronize()
+    barrier()
+
+    stream = torch.cuda.current_stream(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_all0 = torch.cuda.Event(enable_timing=True)
+    t_all1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        t_all0.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            batch.step_greedy(ids, bufs[(args.warmup + i) % ring])
+            ev[i][1].record(stream)
+        t_all1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = t_all0.elapsed_time(t_all1)
+    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([elapsed_ms, kern_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, kern_ms = float(t[0]), float(t[1])
+
+    total_rows = ROWS_PER_GPU * world * args.steps
+    value = total_rows / (elapsed_ms / 1000.0)
+    peak, peak_kind = _peaks()
+    achieved = ROWS_PER_GPU * ALGO_BYTES_PER_ROW_STEP / (kern_ms / 1000.0) / 1e9
+    traffic = _profile_traffic()
+
+    # unfused drop-in path: apply_mask + torch.argmax + commit (3 launches)
+    un_steps = min(args.steps, 64)
+    for i in range(3):
+        lg = bufs[i % ring]
+        batch.apply_mask(ids, lg)
+        batch.commit(ids, lg.argmax(-1))
+    torch.cuda.synchronize()
+    u0 = torch.cuda.Event(enable_timing=True)
+    u1 = torch.cuda.Event(enable_timing=True)
+    u0.record(stream)
+    for i in range(un_steps):
+        lg = bufs[i % ring]
+        batch.apply_mask(ids, lg)
+        batch.commit(ids, lg.argmax(-1))
+    u1.record(stream)
+    torch.cuda.synchronize()
+    un_ms = u0.elapsed_time(u1) / un_steps
+
+    # reference GPU bar: bpdecode's dense torch composite on this B200
+    ref_gpu = _reference_torch_gpu(batch, bufs, ring, device)
+
+    # end to end through the public API with host buffers
+    e2e = _e2e(batch, ids, rank, device, args.e2e_steps, world)
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {**_config(world), "logits_ring": ring,
+                   "ring_note": (f"{ring} pre-generated buffers; step i uses buffer i mod "
+                                 f"{ring}, so after {ring} steps a buffer is reused "
+                                 "(already masked in place)") if ring < args.steps else
+                   "every timed step reads its own fresh buffer"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_kind == "measured" else "fallback 6.65 TB/s",
+                     "kernel": "dense_step_kernel (fused mask+argmax+commit)",
+                     "kernel_ms": kern_ms,
+                     "algo_bytes_per_row_step": ALGO_BYTES_PER_ROW_STEP},
+        "clocks": clocks.summary(),
+        "gpu_launches": args.steps,
+        "e2e": e2e,
+        "unfused_dropin": {"ms_per_step": un_ms, "value": ROWS_PER_GPU * world / (un_ms / 1e3),
+                           "path": "ConstraintBatch.apply_mask + torch.argmax + commit"},
+        "reference_torch_gpu": ref_gpu,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        off, tns, starts = 0, [], []
+        for f in fsas:
+            tn = f.dense_tables()[0].cpu()
+            tns.append(torch.where(tn >= 0, tn + off, tn))
+            starts.append(f.start + off)
+            off += f.num_states
+        line["cpu_baseline"] = cpu_baseline(torch.cat(tns), starts, pats, 32, 24)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _reference_torch_gpu(batch, bufs, ring, device) -> dict:
+    """bpdecode's dense path is torch (ops.py:271-276, 301-306): time that
+    composite on this GPU on the same rows as the GPU bar the kernel beats."""
+    tn = batch._t.tok_next
+    state = batch._state.clone()
+    slots = torch.arange(ROWS_PER_GPU, device=device)
+
+    def step(lg: torch.Tensor) -> None:
+        s = state[slots].long()
+        broken = s < 0
+        rejected = tn.index_select(0, s.clamp(min=0)) == -1
+        rejected |= broken.unsqueeze(1)
+        lg.masked_fill_(rejected, float("-inf"))
+        tok = lg.argmax(-1)
+        nxt = tn[s.clamp(min=0), tok]
+        state[slots] = torch.where(broken, torch.full_like(nxt, -1), nxt)
+
+    n = 16
+    for i in range(3):
+        step(bufs[i % ring])
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n):
+        step(bufs[i % ring])
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / n
+    return {"ms_per_step": ms, "value": ROWS_PER_GPU / (ms / 1e3),
+            "path": "ops.py dense composite (index_select + masked_fill_ + argmax + gather)"}
+
+
+def _e2e(batch, ids, rank, device, steps, world) -> dict:
+    """Same step through the public API from pinned host logits: every step
+    copies its logits host -> device, runs ConstraintBatch.step_greedy and
+    reads the chosen tokens back."""
+    nhost = 2
+    host = [gen_logits(rank, 10_000 + i, device).cpu().pin_memory() for i in range(nhost)]
+    dev = torch.empty(ROWS_PER_GPU, V, dtype=torch.bfloat16, device=device)
+    out = torch.empty(ROWS_PER_GPU, dtype=torch.int64).pin_memory()
+    for i in range(2):
+        dev.copy_(host[i % nhost], non_blocking=True)
+        out.copy_(batch.step_greedy(ids, dev), non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        dev.copy_(host[i % nhost], non_blocking=True)
+        out.copy_(batch.step_greedy(ids, dev), non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t[0])
+    return {"value": ROWS_PER_GPU * world * steps / (ms / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": ROWS_PER_GPU * V * 2, "d2h_bytes_per_step": ROWS_PER_GPU * 8,
+            "steps": steps, "ms_per_step": ms / steps,
+            "path": "pinned host logits -> H2D -> ConstraintBatch.step_greedy -> tokens D2H"}
+
+
+if __name__ == "__main__":
+    main()

@@ -20,21 +20,12 @@
 #include <climits>
 
 #include "common.cuh"
+#include "stream.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace bpd {
 namespace {
-
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kVPT = 4;  // 16-byte vectors per lane per warp tile
-constexpr unsigned kAll = 0xFFFFFFFFu;
-
-template <typename T>
-constexpr int tile_elems() {
-  return 32 * kVPT * Dt<T>::kPerVec;
-}
 
 // ---------------------------------------------------------------------------
 // Table build (compile time).
@@ -97,102 +88,6 @@ __global__ void build_allow_bits_kernel(const int32_t* __restrict__ tok_next, in
   if (w0 + lane < wstride) bits[static_cast<int64_t>(s) * wstride + w0 + lane] = mine;
 }
 
-// ---------------------------------------------------------------------------
-// Per-step streaming over one row segment.
-
-struct ArgState {
-  uint64_t best = 0;                 // packed (key, index) of the best allowed element
-  int32_t first_masked = INT_MAX;    // lowest rejected index seen by this thread
-};
-
-template <typename T, bool kArgmax>
-__device__ __forceinline__ void arg_update(ArgState& st, typename Dt<T>::Bits b, int32_t idx) {
-  if constexpr (kArgmax) {
-    const uint64_t p = pack_arg(order_key(Dt<T>::to_float(b)), idx);
-    st.best = p > st.best ? p : st.best;
-  }
-}
-
-template <bool kArgmax>
-__device__ __forceinline__ void arg_masked(ArgState& st, int32_t idx) {
-  if constexpr (kArgmax) st.first_masked = idx < st.first_masked ? idx : st.first_masked;
-}
-
-// Masks [c0, c1) of `row` (c0 a multiple of the warp tile, so allow words line
-// up) against allow row `brow` (nullptr = reject everything). With kArgmax the
-// thread also tracks the first maximal element of the masked row.
-template <typename T, bool kVec, bool kArgmax>
-__device__ __forceinline__ void mask_range(T* __restrict__ row, int32_t c0, int32_t c1,
-                                           const uint32_t* __restrict__ brow,
-                                           typename Dt<T>::Bits fill, ArgState& st) {
-  using Bits = typename Dt<T>::Bits;
-  constexpr int EPV = Dt<T>::kPerVec;
-  constexpr int TILE = tile_elems<T>();
-  constexpr int WPT = TILE / 32;  // allow words per warp tile
-  constexpr uint32_t FULL = (1u << EPV) - 1u;
-  const int32_t lane = threadIdx.x & 31;
-  const int32_t warp = threadIdx.x >> 5;
-  int32_t vend = c0;
-  if constexpr (kVec) {
-    const int32_t ntiles = c1 > c0 ? (c1 - c0) / TILE : 0;
-    vend = c0 + ntiles * TILE;
-    for (int32_t ti = warp; ti < ntiles; ti += kWarps) {
-      const int32_t tb = c0 + ti * TILE;
-      uint32_t w = 0;
-      if (brow != nullptr && lane < WPT) w = __ldg(brow + (tb >> 5) + lane);
-      uint32_t bits[kVPT];
-#pragma unroll
-      for (int j = 0; j < kVPT; ++j) {
-        const int v = lane + 32 * j;
-        const uint32_t word = __shfl_sync(kAll, w, (v * EPV) >> 5);
-        bits[j] = (word >> ((v * EPV) & 31)) & FULL;
-      }
-      uint4* base = reinterpret_cast<uint4*>(row + tb);
-      uint4 val[kVPT];
-#pragma unroll
-      for (int j = 0; j < kVPT; ++j) {
-        const bool need = kArgmax ? (bits[j] != 0u) : (bits[j] != 0u && bits[j] != FULL);
-        if (need) val[j] = __ldcs(base + lane + 32 * j);
-      }
-#pragma unroll
-      for (int j = 0; j < kVPT; ++j) {
-        const int32_t e0 = tb + (lane + 32 * j) * EPV;
-        if (bits[j] == FULL) {
-          if constexpr (kArgmax) {
-#pragma unroll
-            for (int i = 0; i < EPV; ++i) arg_update<T, true>(st, vec_get<T>(val[j], i), e0 + i);
-          }
-        } else if (bits[j] == 0u) {
-          __stcs(base + lane + 32 * j, vec_splat<T>(fill));
-          arg_masked<kArgmax>(st, e0);
-        } else {
-          __stcs(base + lane + 32 * j, vec_blend<T>(val[j], bits[j], fill));
-          if constexpr (kArgmax) {
-#pragma unroll
-            for (int i = 0; i < EPV; ++i) {
-              if ((bits[j] >> i) & 1u) {
-                arg_update<T, true>(st, vec_get<T>(val[j], i), e0 + i);
-              } else {
-                arg_masked<true>(st, e0 + i);
-              }
-            }
-          }
-        }
-      }
-    }
-  }
-  Bits* rb = reinterpret_cast<Bits*>(row);
-  for (int32_t e = vend + static_cast<int32_t>(threadIdx.x); e < c1; e += kThreads) {
-    const bool allowed = brow != nullptr && ((__ldg(brow + (e >> 5)) >> (e & 31)) & 1u);
-    if (allowed) {
-      if constexpr (kArgmax) arg_update<T, true>(st, rb[e], e);
-    } else {
-      rb[e] = fill;
-      arg_masked<kArgmax>(st, e);
-    }
-  }
-}
-
 __device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__ pool,
                                                      const int64_t* __restrict__ slots,
                                                      int32_t row, const uint32_t* __restrict__ bits,
@@ -220,12 +115,17 @@ __global__ void __launch_bounds__(kThreads)
   mask_range<T, kVec, false>(logits + row * row_stride, c0, c1, brow, fill, st);
 }
 
+// Minimum resident CTAs per SM the fused step is compiled for (register cap).
+#ifndef BPD_STEP_MIN_BLOCKS
+#define BPD_STEP_MIN_BLOCKS 1
+#endif
+
 // Fused greedy step. A thread-block cluster of `k` CTAs owns one row; every
 // CTA masks its slice and reduces its first-maximal element; the partials are
 // written into rank 0's shared memory (distributed shared memory), and after
 // one cluster barrier rank 0 commits the winning token.
 template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
     dense_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V,
                       int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
                       const uint32_t* __restrict__ bits, int32_t wstride,
@@ -247,11 +147,7 @@ __global__ void __launch_bounds__(kThreads)
   ArgState st;
   mask_range<T, kVec, true>(logits + row * row_stride, c0, c1, brow, fill, st);
 
-  uint64_t mine = st.best;
-  if (st.first_masked != INT_MAX) {
-    const uint64_t m = pack_arg(order_key(Dt<T>::to_float(fill)), st.first_masked);
-    mine = m > mine ? m : mine;
-  }
+  uint64_t mine = pack_arg(st.key, st.idx);
   mine = warp_max_u64(mine);
   const int32_t lane = threadIdx.x & 31;
   const int32_t warp = threadIdx.x >> 5;

@@ -1,31 +1,798 @@
-// Pushdown-automaton kernels (placeholder: entry points not yet implemented).
+// Pushdown-automaton (context-free grammar) kernels.
+//
+// Parity contract: the bounded config-set semantics of the reference's
+// pda.hpp:95-258 -- push order, the 8-config / 32-frame caps, the `saturated`
+// flag, the order-preserving dead-config prune and whole-struct copies -- so
+// masks, ok flags and full 266-int config rows are identical.
+//
+// Design.
+// * A config-set lives in shared memory and is worked on by ONE WARP: lane k
+//   owns stack frame k (kPdaMaxDepth = 32 = warp width). Building a candidate
+//   stack, comparing it against every existing config (one vote per config)
+//   and pushing it are all single warp-wide steps instead of 32-iteration
+//   loops over local memory.
+// * Closure runs as a single in-order pass over the growing config list. The
+//   reference runs rounds over [0, n) until no push succeeds; re-visiting an
+//   already-processed config can neither push (its candidates are present, or
+//   were dropped for a full set that never shrinks) nor change `saturated`
+//   (already set), so one pass that keeps going until it reaches the end of
+//   the list performs the same pushes in the same order.
+// * Mask of a row = for every token, does its byte walk keep the set
+//   non-empty. The walk's first step has only 256 outcomes, so each row first
+//   computes which first bytes survive (256 warp walks) and every token whose
+//   first byte dies is rejected without a walk; single-byte survivors are
+//   accepted; only the rest are walked, a warp per token.
+// * Mask memo in HBM, keyed by the config-set's live content (`saturated` and
+//   words outside the live region do not affect the mask and are not part of
+//   the key): an open-addressing table of {hash, canonical 266-int key, packed
+//   allow row}. Rows of a step whose key is present reuse the stored row;
+//   identical misses within one step are de-duplicated so each distinct
+//   config-set is simulated once. The apply pass then streams logits exactly
+//   like the dense path.
+//
+// Per mask call (all on the caller's stream, no host sync):
+//   memset(dedup) -> lookup_kernel -> claim_kernel -> compute_kernel -> apply.
+#include <algorithm>
+
 #include "common.cuh"
+#include "stream.cuh"
+
+namespace bpd {
+namespace {
+
+constexpr int MC = BPD_PDA_MAX_CONFIGS;
+constexpr int MD = BPD_PDA_MAX_DEPTH;
+constexpr int NCFG = BPD_PDA_CONFIG_INTS;
+constexpr int kEps = 0, kByte = 1, kCall = 2;
+constexpr int kProbe = 32;  // memo / dedup probe limit
+
+static_assert(MD == 32, "one lane per stack frame");
+
+__device__ __forceinline__ int32_t& n_of(int32_t* c) { return c[0]; }
+__device__ __forceinline__ int32_t n_of(const int32_t* c) { return c[0]; }
+__device__ __forceinline__ int32_t* st_of(int32_t* c, int i) { return c + 2 + MC + i * MD; }
+__device__ __forceinline__ const int32_t* st_of(const int32_t* c, int i) {
+  return c + 2 + MC + i * MD;
+}
+
+// Is a config equal to the candidate (depth cd; lane k holds frame k) in `c`?
+// pda.hpp:102-108.
+__device__ __forceinline__ bool w_contains(const int32_t* c, int cd, int32_t v, int lane) {
+  const int n = n_of(c);
+  for (int j = 0; j < n; ++j) {
+    if (c[2 + j] != cd) continue;
+    const bool eq = lane >= cd || st_of(c, j)[lane] == v;
+    if (__all_sync(kAll, eq)) return true;
+  }
+  return false;
+}
+
+// pda.hpp:111-121. Caller guarantees all lanes see the same `c` contents.
+__device__ __forceinline__ bool w_push(int32_t* c, int cd, int32_t v, int lane) {
+  const int n = n_of(c);
+  if (n >= MC) {
+    if (lane == 0) c[1] = 1;
+    __syncwarp();
+    return false;
+  }
+  if (lane < cd) st_of(c, n)[lane] = v;
+  if (lane == 0) {
+    c[2 + n] = cd;
+    c[0] = n + 1;
+  }
+  __syncwarp();
+  return true;
+}
+
+__device__ __forceinline__ void w_add(int32_t* c, int cd, int32_t v, int lane) {
+  if (!w_contains(c, cd, v, lane)) w_push(c, cd, v, lane);
+}
+
+// pda.hpp:124-139 -- order-preserving compaction of configs whose top is live.
+__device__ void w_prune(const bpd_pda_grammar& g, int32_t* c, int lane) {
+  const int n = n_of(c);
+  int out = 0;
+  for (int i = 0; i < n; ++i) {
+    const int d = c[2 + i];
+    if (d <= 0) continue;
+    if (!__ldg(g.live + st_of(c, i)[d - 1])) continue;
+    if (out != i) {
+      const int32_t v = lane < d ? st_of(c, i)[lane] : 0;
+      if (lane < d) st_of(c, out)[lane] = v;
+      if (lane == 0) c[2 + out] = d;
+      __syncwarp();
+    }
+    ++out;
+  }
+  if (lane == 0) c[0] = out;
+  __syncwarp();
+}
+
+// pda.hpp:150-198 as one in-order pass (see the file comment).
+__device__ bool w_close(const bpd_pda_grammar& g, int32_t* c, int lane) {
+  for (int i = 0; i < n_of(c); ++i) {
+    const int d = c[2 + i];
+    if (d <= 0) continue;
+    const int32_t mine = lane < d ? st_of(c, i)[lane] : 0;
+    const int32_t top = st_of(c, i)[d - 1];
+    if (__ldg(g.accept + top) && d > 1) w_add(c, d - 1, mine, lane);  // pop
+    const int eb = __ldg(g.edge_offsets + top);
+    const int ee = __ldg(g.edge_offsets + top + 1);
+    for (int e = eb; e < ee; ++e) {
+      const int kind = __ldg(g.edge_kind + e);
+      if (kind == kEps) {
+        const int32_t v = lane == d - 1 ? __ldg(g.edge_dst + e) : mine;
+        w_add(c, d, v, lane);
+      } else if (kind == kCall) {
+        if (d + 1 <= MD) {
+          const int32_t v = lane == d - 1 ? __ldg(g.edge_dst + e)
+                            : lane == d   ? __ldg(g.edge_callee + e)
+                                          : mine;
+          w_add(c, d + 1, v, lane);
+        } else {
+          if (lane == 0) c[1] = 1;
+          __syncwarp();
+        }
+      }
+    }
+  }
+  w_prune(g, c, lane);
+  return n_of(c) > 0;
+}
+
+// pda.hpp:211-236: dst = close(byte-step of src). With kExact the whole 266
+// words of dst are defined exactly as the reference's freshly zeroed `next`
+// (needed when the row is written back); without it only the live region is
+// meaningful, which is all a mask needs.
+template <bool kExact>
+__device__ bool w_advance_byte(const bpd_pda_grammar& g, const int32_t* src, int32_t* dst,
+                               int byte, int lane) {
+  if constexpr (kExact) {
+    for (int k = lane; k < NCFG; k += 32) dst[k] = 0;
+  } else {
+    if (lane == 0) {
+      dst[0] = 0;
+      dst[1] = 0;
+    }
+  }
+  __syncwarp();
+  const int n = n_of(src);
+  for (int i = 0; i < n; ++i) {
+    const int d = src[2 + i];
+    if (d <= 0) continue;
+    const int32_t mine = lane < d ? st_of(src, i)[lane] : 0;
+    const int32_t top = st_of(src, i)[d - 1];
+    const int eb = __ldg(g.edge_offsets + top);
+    const int ee = __ldg(g.edge_offsets + top + 1);
+    for (int e = eb; e < ee; ++e) {
+      if (__ldg(g.edge_kind + e) != kByte) continue;
+      if (byte < __ldg(g.edge_lo + e) || byte > __ldg(g.edge_hi + e)) continue;
+      const int32_t v = lane == d - 1 ? __ldg(g.edge_dst + e) : mine;
+      w_add(dst, d, v, lane);
+    }
+  }
+  if (lane == 0) dst[1] = (dst[1] || src[1]) ? 1 : 0;
+  __syncwarp();
+  return w_close(g, dst, lane);
+}
+
+// pda.hpp:238-244
+__device__ __forceinline__ bool is_complete(const bpd_pda_grammar& g, const int32_t* c) {
+  const int n = n_of(c);
+  for (int i = 0; i < n; ++i)
+    if (c[2 + i] == 1 && st_of(c, i)[0] == g.root_accept) return true;
+  return false;
+}
+
+__device__ __forceinline__ void w_copy(int32_t* dst, const int32_t* src, int lane) {
+  for (int k = lane; k < NCFG; k += 32) dst[k] = src[k];
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// Memo / workspace layout.
+
+struct Memo {
+  uint32_t* tag;    // [cap] 0 = empty, 1 = filled
+  uint64_t* hash;   // [cap]
+  int32_t* key;     // [cap][NCFG] canonical config-sets
+  uint32_t* bits;   // [cap][ws] allow rows
+  int32_t cap;      // power of two, 0 = no memo
+  int32_t ws;       // words per allow row (multiple of 4)
+};
+
+size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+int32_t words_stride(int32_t vocab) { return ((((vocab + 31) / 32) + 3) / 4) * 4; }
+
+Memo memo_view(void* base, int32_t cap, int32_t vocab) {
+  Memo m{};
+  m.cap = base ? cap : 0;
+  m.ws = words_stride(vocab);
+  if (!base) return m;
+  char* p = static_cast<char*>(base);
+  m.tag = reinterpret_cast<uint32_t*>(p);
+  p += align256(sizeof(uint32_t) * cap);
+  m.hash = reinterpret_cast<uint64_t*>(p);
+  p += align256(sizeof(uint64_t) * cap);
+  m.key = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * NCFG * static_cast<size_t>(cap));
+  m.bits = reinterpret_cast<uint32_t*>(p);
+  return m;
+}
+
+size_t memo_bytes(int32_t cap, int32_t vocab) {
+  return align256(sizeof(uint32_t) * cap) + align256(sizeof(uint64_t) * cap) +
+         align256(sizeof(int32_t) * NCFG * static_cast<size_t>(cap)) +
+         align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(cap));
+}
+
+// Row kinds (Work::kind).
+constexpr int32_t kBroken = 0, kHit = 1, kRep = 2, kAlias = 3;
+
+struct Work {
+  int32_t* dedup;    // [dcap] row index + 1 of the representative, 0 = empty
+  int32_t dcap;      // power of two >= 2 * batch
+  int32_t* kind;     // [batch]
+  int32_t* ref;      // [batch] memo entry (kHit, kRep with memo), rep row (kAlias), -1
+  uint64_t* hash;    // [batch]
+  uint32_t* first;   // [batch][8] surviving first bytes (representatives)
+  int32_t* eos_ok;   // [batch]
+  uint32_t* bits;    // [batch][ws] allow rows of representatives without a memo entry
+};
+
+int32_t pow2_at_least(int32_t x) {
+  int32_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+Work work_view(void* base, int32_t batch, int32_t vocab) {
+  Work w{};
+  w.dcap = pow2_at_least(std::max(2 * batch, 2));
+  char* p = static_cast<char*>(base);
+  w.dedup = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * w.dcap);
+  w.kind = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * batch);
+  w.ref = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * batch);
+  w.hash = reinterpret_cast<uint64_t*>(p);
+  p += align256(sizeof(uint64_t) * batch);
+  w.first = reinterpret_cast<uint32_t*>(p);
+  p += align256(sizeof(uint32_t) * 8 * batch);
+  w.eos_ok = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * batch);
+  w.bits = reinterpret_cast<uint32_t*>(p);
+  return w;
+}
+
+size_t work_bytes(int32_t batch, int32_t vocab) {
+  const int32_t dcap = pow2_at_least(std::max(2 * batch, 2));
+  return align256(sizeof(int32_t) * dcap) + 2 * align256(sizeof(int32_t) * batch) +
+         align256(sizeof(uint64_t) * batch) + align256(sizeof(uint32_t) * 8 * batch) +
+         align256(sizeof(int32_t) * batch) +
+         align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(batch));
+}
+
+// murmur3's 64-bit finaliser (a published avalanche mix).
+__device__ __forceinline__ uint64_t fmix64(uint64_t x) {
+  x ^= x >> 33;
+  x *= 0xff51afd7ed558ccdULL;
+  x ^= x >> 33;
+  x *= 0xc4ceb9fe1a85ec53ULL;
+  x ^= x >> 33;
+  return x;
+}
+
+// Hash of the live content (num_configs, depths, frames); position-tagged so
+// config order matters, as it does for the mask under saturation.
+__device__ uint64_t w_hash(const int32_t* c, int lane) {
+  const int n = n_of(c);
+  uint64_t h = 0;
+  for (int i = 0; i < n; ++i) {
+    const int d = c[2 + i];
+    if (lane < d)
+      h ^= fmix64((static_cast<uint64_t>(i * 32 + lane + 1) << 32) ^
+                  static_cast<uint32_t>(st_of(c, i)[lane]));
+    if (lane == 0) h ^= fmix64(0x5bd1e9955bd1e995ULL ^ (static_cast<uint64_t>(i) << 40) ^
+                               static_cast<uint32_t>(d));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) h ^= __shfl_xor_sync(kAll, h, o);
+  return fmix64(h ^ static_cast<uint64_t>(n) * 0x9E3779B97F4A7C15ULL);
+}
+
+// Live-content equality of two config-sets.
+__device__ bool w_same(const int32_t* a, const int32_t* b, int lane) {
+  const int n = n_of(a);
+  if (n != n_of(b)) return false;
+  for (int i = 0; i < n; ++i) {
+    const int d = a[2 + i];
+    if (d != b[2 + i]) return false;
+    const bool eq = lane >= d || st_of(a, i)[lane] == st_of(b, i)[lane];
+    if (!__all_sync(kAll, eq)) return false;
+  }
+  return true;
+}
+
+// Canonical form: live content, `saturated` and everything else zero.
+__device__ void w_canonical(const int32_t* src, int32_t* dst, int lane) {
+  const int n = n_of(src);
+  for (int k = lane; k < NCFG; k += 32) {
+    int32_t v = 0;
+    if (k == 0) {
+      v = n;
+    } else if (k >= 2 && k < 2 + MC) {
+      v = (k - 2) < n ? src[k] : 0;
+    } else if (k >= 2 + MC) {
+      const int i = (k - 2 - MC) / MD, f = (k - 2 - MC) % MD;
+      v = (i < n && f < src[2 + i]) ? src[k] : 0;
+    }
+    dst[k] = v;
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ int64_t slot_of(const int64_t* slots, int32_t b) {
+  return slots ? slots[b] : b;
+}
+
+// ---------------------------------------------------------------------------
+// Mask pipeline.
+
+// One CTA per row: memo lookup and in-batch dedup (warp 0), then the
+// surviving-first-byte table of representatives (all warps).
+__global__ void __launch_bounds__(kThreads)
+    lookup_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
+                  const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
+                  Memo memo, Work w) {
+  __shared__ int32_t base[NCFG];
+  __shared__ int32_t scratch[kWarps][NCFG];
+  __shared__ int32_t s_kind;
+  const int32_t b = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t slot = slot_of(slots, b);
+  if (broken && broken[slot]) {
+    if (threadIdx.x == 0) {
+      w.kind[b] = kBroken;
+      w.ref[b] = -1;
+    }
+    return;
+  }
+  const int32_t* row = pool + slot * NCFG;
+  for (int k = threadIdx.x; k < NCFG; k += kThreads) base[k] = row[k];
+  __syncthreads();
+  if (warp == 0) {
+    const uint64_t h = w_hash(base, lane);
+    int32_t kind = kRep, ref = -1;
+    // memo (read-only in this kernel)
+    for (int p = 0; memo.cap && p < kProbe; ++p) {
+      const int32_t e = static_cast<int32_t>((h + p) & (memo.cap - 1));
+      if (memo.tag[e] == 0) break;
+      if (memo.hash[e] == h && w_same(base, memo.key + static_cast<int64_t>(e) * NCFG, lane)) {
+        kind = kHit;
+        ref = e;
+        break;
+      }
+    }
+    if (kind != kHit) {
+      // in-batch dedup: the first row to claim a dedup slot for this content
+      // is the representative; equal rows become its aliases
+      for (int p = 0; p < w.dcap; ++p) {
+        const int32_t d = static_cast<int32_t>((h + p) & (w.dcap - 1));
+        int32_t prev = 0;
+        if (lane == 0) prev = atomicCAS(w.dedup + d, 0, b + 1);
+        prev = __shfl_sync(kAll, prev, 0);
+        if (prev == 0) break;  // representative
+        const int32_t other = prev - 1;
+        const int32_t* orow = pool + slot_of(slots, other) * NCFG;
+        if (w_same(base, orow, lane)) {
+          kind = kAlias;
+          ref = other;
+          break;
+        }
+      }
+    }
+    if (lane == 0) {
+      w.kind[b] = kind;
+      w.ref[b] = ref;
+      w.hash[b] = h;
+      s_kind = kind;
+    }
+  }
+  __syncthreads();
+  if (s_kind != kRep) return;
+  // which first bytes keep the set alive: 32 bytes per warp
+  int32_t* tmp = scratch[warp];
+  uint32_t word = 0;
+  for (int j = 0; j < 32; ++j) {
+    const int byte = warp * 32 + j;
+    const bool ok = w_advance_byte<false>(g, base, tmp, byte, lane);
+    if (ok) word |= 1u << j;
+  }
+  if (lane == 0) w.first[static_cast<int64_t>(b) * 8 + warp] = word;
+  if (threadIdx.x == 0) w.eos_ok[b] = is_complete(g, base) ? 1 : 0;
+}
+
+// Representatives claim a memo entry (after every lookup of this call has
+// finished, so no lookup can observe a half-written entry).
+__global__ void claim_kernel(const int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
+                             int32_t batch, Memo memo, Work w) {
+  const int lane = threadIdx.x & 31;
+  const int32_t b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (b >= batch) return;
+  if (w.kind[b] != kRep) return;
+  if (memo.cap == 0) return;
+  const uint64_t h = w.hash[b];
+  int32_t got = -1;
+  for (int p = 0; p < kProbe; ++p) {
+    const int32_t e = static_cast<int32_t>((h + p) & (memo.cap - 1));
+    uint32_t prev = 0;
+    if (lane == 0) prev = atomicCAS(memo.tag + e, 0u, 1u);
+    prev = __shfl_sync(kAll, prev, 0);
+    if (prev == 0) {
+      got = e;
+      break;
+    }
+  }
+  if (got < 0) return;  // table full along this probe: bits go to the workspace
+  const int32_t* row = pool + slot_of(slots, b) * NCFG;
+  w_canonical(row, memo.key + static_cast<int64_t>(got) * NCFG, lane);
+  if (lane == 0) {
+    memo.hash[got] = h;
+    w.ref[b] = got;
+  }
+}
+
+__device__ __forceinline__ uint32_t* rep_bits(const Memo& memo, const Work& w, int32_t b) {
+  const int32_t e = w.ref[b];
+  if (memo.cap && e >= 0) return memo.bits + static_cast<int64_t>(e) * memo.ws;
+  return w.bits + static_cast<int64_t>(b) * memo.ws;
+}
+
+// Allow bits of every representative row: a CTA owns `chunk` tokens of one
+// row; each warp decides 32 tokens at a time (lane = token), walking only the
+// ones whose first byte survives and that are longer than one byte.
+__global__ void __launch_bounds__(kThreads)
+    compute_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
+                   const int64_t* __restrict__ slots, Memo memo, Work w, int32_t chunk,
+                   int32_t chunks_per_row) {
+  __shared__ int32_t base[NCFG];
+  __shared__ int32_t buf[kWarps][2][NCFG];
+  __shared__ uint32_t first[8];
+  const int32_t b = blockIdx.x / chunks_per_row;
+  if (w.kind[b] != kRep) return;
+  const int32_t c0 = (blockIdx.x - b * chunks_per_row) * chunk;
+  const int32_t V = g.vocab_size;
+  const int32_t c1 = min(V, c0 + chunk);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int32_t* row = pool + slot_of(slots, b) * NCFG;
+  for (int k = threadIdx.x; k < NCFG; k += kThreads) base[k] = row[k];
+  if (threadIdx.x < 8) first[threadIdx.x] = w.first[static_cast<int64_t>(b) * 8 + threadIdx.x];
+  __syncthreads();
+  const bool eos_ok = w.eos_ok[b] != 0;
+  const bool nonempty = n_of(base) > 0;
+  uint32_t* out = rep_bits(memo, w, b);
+  for (int32_t t0 = c0 + warp * 32; t0 < c1; t0 += kWarps * 32) {
+    const int32_t t = t0 + lane;
+    bool ok = false, walk = false;
+    int32_t o0 = 0, o1 = 0;
+    if (t < c1) {
+      if (t == g.eos_id) {
+        ok = eos_ok;
+      } else {
+        o0 = __ldg(g.tok_offsets + t);
+        o1 = __ldg(g.tok_offsets + t + 1);
+        if (o0 == o1) {
+          ok = nonempty;
+        } else {
+          const int fb = __ldg(g.tok_bytes + o0);
+          if ((first[fb >> 5] >> (fb & 31)) & 1u) {
+            if (o1 - o0 == 1) ok = true;
+            else walk = true;
+          }
+        }
+      }
+    }
+    uint32_t todo = __ballot_sync(kAll, walk);
+    while (todo) {
+      const int j = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int32_t s = __shfl_sync(kAll, o0, j);
+      const int32_t e = __shfl_sync(kAll, o1, j);
+      const int32_t* cur = base;
+      int which = 0;
+      bool alive = true;
+      for (int32_t i = s; i < e && alive; ++i) {
+        int32_t* nxt = buf[warp][which];
+        alive = w_advance_byte<false>(g, cur, nxt, __ldg(g.tok_bytes + i), lane);
+        cur = nxt;
+        which ^= 1;
+      }
+      if (lane == j) ok = alive;
+    }
+    const uint32_t word = __ballot_sync(kAll, ok);
+    if (lane == 0) out[t0 >> 5] = word;
+  }
+}
+
+__device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work& w, int32_t b) {
+  const int32_t kind = w.kind[b];
+  if (kind == kBroken) return nullptr;
+  if (kind == kHit) return memo.bits + static_cast<int64_t>(w.ref[b]) * memo.ws;
+  const int32_t rep = kind == kAlias ? w.ref[b] : b;
+  return rep_bits(memo, w, rep);
+}
+
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(kThreads)
+    pda_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Memo memo, Work w,
+                     typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
+  const int32_t row = blockIdx.x / chunks_per_row;
+  const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
+  const int32_t c1 = min(V, c0 + chunk);
+  ArgState st;
+  mask_range<T, kVec, false>(logits + row * row_stride, c0, c1, row_bits(memo, w, row), fill,
+                             st);
+}
+
+__global__ void pda_bits_out_kernel(int32_t W, Memo memo, Work w, uint32_t* __restrict__ out) {
+  const int32_t row = blockIdx.y;
+  const uint32_t* src = row_bits(memo, w, row);
+  for (int32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < W; i += gridDim.x * blockDim.x)
+    out[static_cast<int64_t>(row) * W + i] = src ? src[i] : 0u;
+}
+
+// ---------------------------------------------------------------------------
+// Commit, init, completeness.
+
+constexpr int kAdvWarps = 4;
+
+// One warp per row: the exact byte walk of pda_cpu.cpp:35-54 in shared memory;
+// the final config-set is written back only if the token was accepted.
+__global__ void __launch_bounds__(kAdvWarps * 32)
+    advance_kernel(bpd_pda_grammar g, int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
+                   int32_t batch, const void* __restrict__ tokens, int32_t tokens64,
+                   uint8_t* __restrict__ ok_out, uint8_t* __restrict__ broken,
+                   int32_t* __restrict__ status_out) {
+  __shared__ int32_t buf[kAdvWarps][3][NCFG];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int32_t b = blockIdx.x * kAdvWarps + warp;
+  if (b >= batch) return;
+  const int64_t slot = slot_of(slots, b);
+  int32_t* row = pool + slot * NCFG;
+  const int64_t t = tokens64 ? static_cast<const int64_t*>(tokens)[b]
+                             : static_cast<int64_t>(static_cast<const int32_t*>(tokens)[b]);
+  int32_t* trial = buf[warp][0];
+  w_copy(trial, row, lane);
+  bool ok;
+  if (t == g.eos_id) {
+    ok = is_complete(g, trial);  // EOS never changes the config-set
+  } else if (t < 0 || t >= g.vocab_size) {
+    ok = false;
+  } else {
+    const int32_t s = __ldg(g.tok_offsets + t), e = __ldg(g.tok_offsets + t + 1);
+    const int32_t* cur = trial;
+    int which = 1;
+    ok = true;
+    for (int32_t i = s; i < e && ok; ++i) {
+      int32_t* nxt = buf[warp][which];
+      ok = w_advance_byte<true>(g, cur, nxt, __ldg(g.tok_bytes + i), lane);
+      cur = nxt;
+      which = which == 1 ? 2 : 1;
+    }
+    if (ok && cur != trial) {
+      for (int k = lane; k < NCFG; k += 32) row[k] = cur[k];
+    }
+  }
+  if (lane == 0) {
+    if (ok_out) ok_out[b] = ok ? 1 : 0;
+    if (broken) {
+      const uint8_t br = static_cast<uint8_t>(broken[slot] | (ok ? 0 : 1));
+      broken[slot] = br;
+      if (status_out) status_out[b] = br ? -1 : 1;
+    } else if (status_out) {
+      status_out[b] = ok ? 1 : -1;
+    }
+  }
+}
+
+// pda.hpp:200-207 on a zeroed struct (as the reference's pda_init op).
+__global__ void init_kernel(bpd_pda_grammar g, int32_t* __restrict__ out) {
+  __shared__ int32_t c[NCFG];
+  const int lane = threadIdx.x;
+  for (int k = lane; k < NCFG; k += 32) c[k] = 0;
+  __syncwarp();
+  w_push(c, 1, lane == 0 ? g.root_start : 0, lane);
+  w_close(g, c, lane);
+  for (int k = lane; k < NCFG; k += 32) out[k] = c[k];
+}
+
+__global__ void complete_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
+                                const int64_t* __restrict__ slots,
+                                const uint8_t* __restrict__ broken, int32_t batch,
+                                uint8_t* __restrict__ out) {
+  const int32_t b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const int64_t slot = slot_of(slots, b);
+  out[b] = (!(broken && broken[slot]) && is_complete(g, pool + slot * NCFG)) ? 1 : 0;
+}
+
+bpd_status check_grammar(const bpd_pda_grammar* g) {
+  BPD_REQUIRE(g != nullptr, "null grammar");
+  BPD_REQUIRE(g->accept && g->live && g->edge_offsets && g->tok_offsets && g->tok_bytes,
+              "grammar: null table pointer");
+  BPD_REQUIRE(g->num_edges == 0 || (g->edge_kind && g->edge_lo && g->edge_hi && g->edge_dst &&
+                                    g->edge_callee),
+              "grammar: null edge pointer");
+  BPD_REQUIRE(g->num_states > 0 && g->vocab_size > 0, "grammar: bad sizes");
+  BPD_REQUIRE(g->root_start >= 0 && g->root_start < g->num_states, "grammar: bad root_start");
+  return BPD_OK;
+}
+
+// memset(dedup) + lookup + claim + compute: leaves every row's allow bits
+// resolvable through (memo, work).
+bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, const int64_t* slots,
+                             const uint8_t* broken, int32_t batch, void* memo_mem, int32_t cap,
+                             void* workspace, Memo* memo_out, Work* work_out, cudaStream_t st) {
+  bpd_status rc = check_grammar(g);
+  if (rc) return rc;
+  BPD_REQUIRE(pool && workspace, "null config pool or workspace");
+  BPD_REQUIRE(memo_mem == nullptr || (cap > 0 && (cap & (cap - 1)) == 0),
+              "memo capacity must be a power of two");
+  Memo memo = memo_view(memo_mem, cap, g->vocab_size);
+  Work w = work_view(workspace, batch, g->vocab_size);
+  cudaError_t e = cudaMemsetAsync(w.dedup, 0, sizeof(int32_t) * w.dcap, st);
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memset dedup: %s", cudaGetErrorString(e));
+  lookup_kernel<<<batch, kThreads, 0, st>>>(*g, pool, slots, broken, memo, w);
+  rc = check_launch("pda lookup_kernel");
+  if (rc) return rc;
+  claim_kernel<<<(batch * 32 + 127) / 128, 128, 0, st>>>(pool, slots, batch, memo, w);
+  rc = check_launch("pda claim_kernel");
+  if (rc) return rc;
+  const int32_t chunk = kWarps * 32 * 16;  // 4096 tokens per CTA
+  const int32_t chunks = (g->vocab_size + chunk - 1) / chunk;
+  const int64_t grid = static_cast<int64_t>(batch) * chunks;
+  BPD_REQUIRE(grid < 0x7FFFFFFF, "batch too large");
+  compute_kernel<<<static_cast<unsigned>(grid), kThreads, 0, st>>>(*g, pool, slots, memo, w,
+                                                                   chunk, chunks);
+  rc = check_launch("pda compute_kernel");
+  if (rc) return rc;
+  *memo_out = memo;
+  *work_out = w;
+  return BPD_OK;
+}
+
+template <typename T>
+bpd_status launch_pda_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
+                            const Memo& memo, const Work& w, float neg_inf, cudaStream_t st) {
+  constexpr int TILE = tile_elems<T>();
+  const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+  const int32_t chunk = TILE * kWarps * 2;
+  const int32_t chunks = (V + chunk - 1) / chunk;
+  const int64_t grid = static_cast<int64_t>(batch) * chunks;
+  BPD_REQUIRE(grid < 0x7FFFFFFF, "batch too large");
+  const auto fill = Dt<T>::from_float_host(neg_inf);
+  T* lg = static_cast<T*>(logits);
+  if (vec) {
+    pda_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+        lg, row_stride, V, memo, w, fill, chunk, chunks);
+  } else {
+    pda_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+        lg, row_stride, V, memo, w, fill, chunk, chunks);
+  }
+  return check_launch("pda_apply_kernel");
+}
+
+}  // namespace
+}  // namespace bpd
 
 using namespace bpd;
 
-extern "C" bpd_status bpd_pda_init(const bpd_pda_grammar*, int32_t*, void*) {
-  return fail(BPD_ERR_INVALID, "bpd_pda_init: not implemented");
+extern "C" bpd_status bpd_pda_init(const bpd_pda_grammar* g, int32_t* config_out, void* stream) {
+  bpd_status rc = check_grammar(g);
+  if (rc) return rc;
+  BPD_REQUIRE(config_out != nullptr, "bpd_pda_init: null output");
+  init_kernel<<<1, 32, 0, as_stream(stream)>>>(*g, config_out);
+  return check_launch("pda init_kernel");
 }
-extern "C" size_t bpd_pda_memo_bytes(int32_t, int32_t) { return 0; }
-extern "C" bpd_status bpd_pda_memo_reset(void*, int32_t, int32_t, void*) {
-  return fail(BPD_ERR_INVALID, "bpd_pda_memo_reset: not implemented");
+
+extern "C" size_t bpd_pda_memo_bytes(int32_t capacity, int32_t vocab_size) {
+  if (capacity <= 0 || vocab_size <= 0) return 0;
+  return memo_bytes(capacity, vocab_size);
 }
-extern "C" size_t bpd_pda_workspace_bytes(int32_t, int32_t) { return 0; }
-extern "C" bpd_status bpd_pda_mask_bits(const bpd_pda_grammar*, const int32_t*, const int64_t*,
-                                        const uint8_t*, int32_t, void*, int32_t, void*, uint32_t*,
-                                        void*) {
-  return fail(BPD_ERR_INVALID, "bpd_pda_mask_bits: not implemented");
+
+extern "C" bpd_status bpd_pda_memo_reset(void* memo, int32_t capacity, int32_t vocab_size,
+                                         void* stream) {
+  BPD_REQUIRE(memo != nullptr, "bpd_pda_memo_reset: null memo");
+  BPD_REQUIRE(capacity > 0 && (capacity & (capacity - 1)) == 0,
+              "bpd_pda_memo_reset: capacity must be a power of two");
+  BPD_REQUIRE(vocab_size > 0, "bpd_pda_memo_reset: bad vocab");
+  Memo m = memo_view(memo, capacity, vocab_size);
+  const cudaError_t e = cudaMemsetAsync(m.tag, 0, sizeof(uint32_t) * capacity, as_stream(stream));
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memo reset: %s", cudaGetErrorString(e));
+  return BPD_OK;
 }
-extern "C" bpd_status bpd_pda_apply_mask(const bpd_pda_grammar*, void*, int32_t, int64_t,
-                                         const int32_t*, const int64_t*, const uint8_t*, int32_t,
-                                         void*, int32_t, void*, float, void*) {
-  return fail(BPD_ERR_INVALID, "bpd_pda_apply_mask: not implemented");
+
+extern "C" size_t bpd_pda_workspace_bytes(int32_t batch, int32_t vocab_size) {
+  if (batch <= 0 || vocab_size <= 0) return 256;
+  return work_bytes(batch, vocab_size);
 }
-extern "C" bpd_status bpd_pda_advance(const bpd_pda_grammar*, int32_t*, const int64_t*, int32_t,
-                                      const void*, int32_t, uint8_t*, uint8_t*, int32_t*, void*) {
-  return fail(BPD_ERR_INVALID, "bpd_pda_advance: not implemented");
+
+extern "C" bpd_status bpd_pda_mask_bits(const bpd_pda_grammar* g, const int32_t* config_pool,
+                                        const int64_t* slots, const uint8_t* broken,
+                                        int32_t batch, void* memo, int32_t memo_capacity,
+                                        void* workspace, uint32_t* out_bits, void* stream) {
+  BPD_REQUIRE(batch >= 0, "bpd_pda_mask_bits: bad batch");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(out_bits != nullptr, "bpd_pda_mask_bits: null output");
+  BPD_REQUIRE(batch <= 65535, "bpd_pda_mask_bits: batch > 65535");
+  cudaStream_t st = as_stream(stream);
+  Memo m;
+  Work w;
+  bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
+                                    workspace, &m, &w, st);
+  if (rc) return rc;
+  const int32_t W = (g->vocab_size + 31) / 32;
+  dim3 grid((W + 255) / 256, batch);
+  pda_bits_out_kernel<<<grid, 256, 0, st>>>(W, m, w, out_bits);
+  return check_launch("pda_bits_out_kernel");
 }
-extern "C" bpd_status bpd_pda_is_complete(const bpd_pda_grammar*, const int32_t*, const int64_t*,
-                                          const uint8_t*, int32_t, uint8_t*, void*) {
-  return fail(BPD_ERR_INVALID, "bpd_pda_is_complete: not implemented");
+
+extern "C" bpd_status bpd_pda_apply_mask(const bpd_pda_grammar* g, void* logits, int32_t dtype,
+                                         int64_t row_stride, const int32_t* config_pool,
+                                         const int64_t* slots, const uint8_t* broken,
+                                         int32_t batch, void* memo, int32_t memo_capacity,
+                                         void* workspace, float neg_inf, void* stream) {
+  BPD_REQUIRE(batch >= 0, "bpd_pda_apply_mask: bad batch");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(logits != nullptr, "bpd_pda_apply_mask: null logits");
+  BPD_REQUIRE(g && row_stride >= g->vocab_size, "bpd_pda_apply_mask: row_stride < vocab");
+  cudaStream_t st = as_stream(stream);
+  Memo m;
+  Work w;
+  bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
+                                    workspace, &m, &w, st);
+  if (rc) return rc;
+  switch (dtype) {
+    case BPD_F32:
+      return launch_pda_apply<float>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf, st);
+    case BPD_BF16:
+      return launch_pda_apply<__nv_bfloat16>(logits, row_stride, batch, g->vocab_size, m, w,
+                                             neg_inf, st);
+    case BPD_F16:
+      return launch_pda_apply<__half>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
+                                      st);
+    default:
+      return fail(BPD_ERR_INVALID, "bpd_pda_apply_mask: unsupported logits dtype %d", dtype);
+  }
+}
+
+extern "C" bpd_status bpd_pda_advance(const bpd_pda_grammar* g, int32_t* config_pool,
+                                      const int64_t* slots, int32_t batch, const void* tokens,
+                                      int32_t tokens_int64, uint8_t* ok_out, uint8_t* broken,
+                                      int32_t* status_out, void* stream) {
+  bpd_status rc = check_grammar(g);
+  if (rc) return rc;
+  BPD_REQUIRE(batch >= 0, "bpd_pda_advance: bad batch");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(config_pool && tokens, "bpd_pda_advance: null pointer");
+  const int32_t blocks = (batch + kAdvWarps - 1) / kAdvWarps;
+  advance_kernel<<<blocks, kAdvWarps * 32, 0, as_stream(stream)>>>(
+      *g, config_pool, slots, batch, tokens, tokens_int64, ok_out, broken, status_out);
+  return check_launch("pda advance_kernel");
+}
+
+extern "C" bpd_status bpd_pda_is_complete(const bpd_pda_grammar* g, const int32_t* config_pool,
+                                          const int64_t* slots, const uint8_t* broken,
+                                          int32_t batch, uint8_t* complete_out, void* stream) {
+  bpd_status rc = check_grammar(g);
+  if (rc) return rc;
+  BPD_REQUIRE(batch >= 0, "bpd_pda_is_complete: bad batch");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(config_pool && complete_out, "bpd_pda_is_complete: null pointer");
+  complete_kernel<<<(batch + 127) / 128, 128, 0, as_stream(stream)>>>(*g, config_pool, slots,
+                                                                      broken, batch, complete_out);
+  return check_launch("pda complete_kernel");
 }
