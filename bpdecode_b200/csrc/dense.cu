@@ -100,8 +100,17 @@ __device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__
   return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
 }
 
+// Register cap of the streaming kernels (resident CTAs per SM) and warp tiles
+// per warp of one apply CTA; tuned on B200.
+#ifndef BPD_APPLY_MIN_BLOCKS
+#define BPD_APPLY_MIN_BLOCKS 8
+#endif
+#ifndef BPD_APPLY_TILES_PER_WARP
+#define BPD_APPLY_TILES_PER_WARP 4
+#endif
+
 template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
     dense_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V,
                        const int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
                        const uint32_t* __restrict__ bits, int32_t wstride, int32_t S,
@@ -111,13 +120,14 @@ __global__ void __launch_bounds__(kThreads)
   const int32_t c1 = min(V, c0 + chunk);
   int32_t s;
   const uint32_t* brow = state_row(pool, slots, row, bits, wstride, S, &s, nullptr);
+  extern __shared__ __align__(16) uint8_t smem[];
   ArgState st;
-  mask_range<T, kVec, false>(logits + row * row_stride, c0, c1, brow, fill, st);
+  mask_chunk<T, kVec, false>(logits + row * row_stride, c0, c1, brow, fill, st, smem);
 }
 
 // Minimum resident CTAs per SM the fused step is compiled for (register cap).
 #ifndef BPD_STEP_MIN_BLOCKS
-#define BPD_STEP_MIN_BLOCKS 1
+#define BPD_STEP_MIN_BLOCKS 8
 #endif
 
 // Fused greedy step. A thread-block cluster of `k` CTAs owns one row; every
@@ -144,8 +154,9 @@ __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
   int64_t slot;
   const uint32_t* brow = state_row(pool, slots, row, bits, wstride, S, &s, &slot);
 
+  extern __shared__ __align__(16) uint8_t smem[];
   ArgState st;
-  mask_range<T, kVec, true>(logits + row * row_stride, c0, c1, brow, fill, st);
+  mask_chunk<T, kVec, true>(logits + row * row_stride, c0, c1, brow, fill, st, smem);
 
   uint64_t mine = pack_arg(st.key, st.idx);
   mine = warp_max_u64(mine);
@@ -214,27 +225,26 @@ bpd_status launch_apply(void* logits, int64_t row_stride, int32_t batch, int32_t
                         int32_t wstride, int32_t S, float neg_inf, cudaStream_t st) {
   constexpr int TILE = tile_elems<T>();
   const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-  // ~2 warp tiles per warp per CTA: fine-grained enough to balance rows of
-  // different masks across 148 SMs.
-  const int32_t chunk = TILE * kWarps * 2;
+  const int32_t chunk = TILE * kWarps * BPD_APPLY_TILES_PER_WARP;
   const int32_t chunks = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * chunks;
   BPD_REQUIRE(grid < INT_MAX, "batch too large");
   const auto fill = Dt<T>::from_float_host(neg_inf);
+  const size_t smem = stream_smem_bytes<T>(chunk);
   T* lg = static_cast<T*>(logits);
   if (vec) {
-    dense_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+    dense_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
         lg, row_stride, V, pool, slots, bits, wstride, S, fill, chunk, chunks);
   } else {
-    dense_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+    dense_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
         lg, row_stride, V, pool, slots, bits, wstride, S, fill, chunk, chunks);
   }
   return check_launch("dense_apply_kernel");
 }
 
 int32_t auto_ctas_per_row(int32_t batch) {
-  // aim for >= ~6 resident CTAs per SM across the 148 SMs
-  const int32_t want = (148 * 6 + batch - 1) / batch;
+  // aim for ~1.5 waves of 8 resident CTAs on each of the 148 SMs
+  const int32_t want = (148 * 12 + batch - 1) / batch;
   int32_t k = 1;
   while (k < want && k < 8) k <<= 1;
   return k;
@@ -255,7 +265,9 @@ bpd_status launch_step(void* logits, int64_t row_stride, int32_t batch, int32_t 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = stream_smem_bytes<T>(chunk);
+  BPD_REQUIRE(cfg.dynamicSmemBytes <= 48 * 1024,
+              "bpd_dense_step_greedy: vocab too large for %d CTAs per row", k);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

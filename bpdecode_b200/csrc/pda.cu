@@ -526,15 +526,16 @@ __device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work
 }
 
 template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 8)
     pda_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Memo memo, Work w,
                      typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
   const int32_t row = blockIdx.x / chunks_per_row;
   const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
   const int32_t c1 = min(V, c0 + chunk);
+  extern __shared__ __align__(16) uint8_t smem[];
   ArgState st;
-  mask_range<T, kVec, false>(logits + row * row_stride, c0, c1, row_bits(memo, w, row), fill,
-                             st);
+  mask_chunk<T, kVec, false>(logits + row * row_stride, c0, c1, row_bits(memo, w, row), fill,
+                             st, smem);
 }
 
 __global__ void pda_bits_out_kernel(int32_t W, Memo memo, Work w, uint32_t* __restrict__ out) {
@@ -669,17 +670,18 @@ bpd_status launch_pda_apply(void* logits, int64_t row_stride, int32_t batch, int
                             const Memo& memo, const Work& w, float neg_inf, cudaStream_t st) {
   constexpr int TILE = tile_elems<T>();
   const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-  const int32_t chunk = TILE * kWarps * 2;
+  const int32_t chunk = TILE * kWarps * 4;
   const int32_t chunks = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * chunks;
   BPD_REQUIRE(grid < 0x7FFFFFFF, "batch too large");
   const auto fill = Dt<T>::from_float_host(neg_inf);
+  const size_t smem = stream_smem_bytes<T>(chunk);
   T* lg = static_cast<T*>(logits);
   if (vec) {
-    pda_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+    pda_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
         lg, row_stride, V, memo, w, fill, chunk, chunks);
   } else {
-    pda_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+    pda_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
         lg, row_stride, V, memo, w, fill, chunk, chunks);
   }
   return check_launch("pda_apply_kernel");

@@ -49,24 +49,55 @@ __device__ __forceinline__ uint32_t vec_max_key(const uint4& v) {
 }
 
 // Fold the vector starting at element e0 into the running best: only a vector
-// whose maximum beats the best so far is searched for its first maximal lane.
+// whose maximum is at least the best so far is searched for its first
+// maximal lane. Ties go to the lower index, whatever order elements are seen.
 template <typename T>
 __device__ __forceinline__ void arg_vec(ArgState& st, const uint4& v, int32_t e0) {
   const uint32_t k = vec_max_key<T>(v);
-  if (k > st.key) {
+  if (k >= st.key) {
     int32_t first = 0;
 #pragma unroll
     for (int i = Dt<T>::kPerVec - 1; i >= 0; --i)
       if (order_key(Dt<T>::to_float(vec_get<T>(v, i))) == k) first = i;
-    st.key = k;
-    st.idx = e0 + first;
+    if (k > st.key || e0 + first < st.idx) {
+      st.key = k;
+      st.idx = e0 + first;
+    }
   }
 }
 
 __device__ __forceinline__ void arg_one(ArgState& st, uint32_t k, int32_t idx) {
-  if (k > st.key) {
+  if (k > st.key || (k == st.key && idx < st.idx)) {
     st.key = k;
     st.idx = idx;
+  }
+}
+
+// Shared memory of one streaming CTA: a buffer of fill values that bulk
+// stores copy from, one flag byte per warp tile, then the staged allow words.
+constexpr int32_t kFillBytes = 8192;
+
+template <typename T>
+__host__ __device__ constexpr int32_t stream_tiles(int32_t chunk) {
+  return (chunk + tile_elems<T>() - 1) / tile_elems<T>();
+}
+
+template <typename T>
+__host__ __device__ constexpr size_t stream_smem_bytes(int32_t chunk) {
+  return kFillBytes + ((static_cast<size_t>(stream_tiles<T>(chunk)) + 15) & ~static_cast<size_t>(15)) +
+         sizeof(uint32_t) * static_cast<size_t>((chunk + 31) / 32 + 1);
+}
+
+// Bulk (TMA engine) store of `bytes` (a multiple of 16) of fill values to a
+// 16-byte aligned global address, in pieces of at most kFillBytes.
+__device__ __forceinline__ void bulk_fill(void* dst, uint32_t bytes, const uint4* sfill) {
+  const uint32_t src = static_cast<uint32_t>(__cvta_generic_to_shared(sfill));
+  char* d = static_cast<char*>(dst);
+  for (uint32_t off = 0; off < bytes; off += kFillBytes) {
+    const uint32_t n = min(static_cast<uint32_t>(kFillBytes), bytes - off);
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(d + off),
+                 "r"(src), "r"(n)
+                 : "memory");
   }
 }
 
@@ -74,32 +105,81 @@ __device__ __forceinline__ void arg_one(ArgState& st, uint32_t k, int32_t idx) {
 // up) against allow row `brow` (nullptr = reject everything). With kArgmax the
 // thread also tracks the first maximal element of the masked row (rejected
 // elements count with the fill value, exactly as torch.argmax sees the row).
+//
+// 1. The chunk's allow words are staged into shared memory with independent
+//    loads (one latency for the chunk, not one dependent L2 trip per tile).
+// 2. Tiles (TILE elements) with no allowed token are flagged; thread 0 writes
+//    every run of them with the bulk-copy (TMA) engine from a buffer of fill
+//    values -- no per-element instructions -- and only waits for the engine
+//    to have read the buffer before the CTA may exit.
+// 3. The other tiles stream through registers, interleaved across warps so a
+//    CTA's accesses stay within one window: all-allowed vectors are skipped
+//    (loaded only for the argmax), rejected vectors stored, mixed ones loaded,
+//    blended and stored.
 // Elements are visited in increasing order per thread, so a strict `>` keeps
-// the first occurrence.
+// the first occurrence. All threads of the CTA must call this.
 template <typename T, bool kVec, bool kArgmax>
-__device__ __forceinline__ void mask_range(T* __restrict__ row, int32_t c0, int32_t c1,
+__device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int32_t c1,
                                            const uint32_t* __restrict__ brow,
-                                           typename Dt<T>::Bits fill, ArgState& st) {
+                                           typename Dt<T>::Bits fill, ArgState& st,
+                                           uint8_t* __restrict__ smem) {
   using Bits = typename Dt<T>::Bits;
   constexpr int EPV = Dt<T>::kPerVec;
   constexpr int TILE = tile_elems<T>();
   constexpr int WPT = TILE / 32;  // allow words per warp tile
   constexpr uint32_t FULL = (1u << EPV) - 1u;
+  uint4* sfill = reinterpret_cast<uint4*>(smem);
+  uint8_t* sdead = smem + kFillBytes;
   const int32_t lane = threadIdx.x & 31;
   const int32_t warp = threadIdx.x >> 5;
   const uint32_t fill_key = kArgmax ? order_key(Dt<T>::to_float(fill)) : 0u;
+  const uint4 fv = vec_splat<T>(fill);
+  const int32_t ntiles = (kVec && c1 > c0) ? (c1 - c0) / TILE : 0;
+  uint32_t* sbits = reinterpret_cast<uint32_t*>(
+      smem + kFillBytes + ((static_cast<size_t>(stream_tiles<T>(c1 - c0 > 0 ? c1 - c0 : 0)) + 15) &
+                           ~static_cast<size_t>(15)));
+  const int32_t w0 = c0 >> 5;
+  const int32_t nw = c1 > c0 ? ((c1 + 31) >> 5) - w0 : 0;
+  if (brow != nullptr) {
+    for (int32_t i = threadIdx.x; i < nw; i += kThreads) sbits[i] = __ldg(brow + w0 + i);
+  }
+  if constexpr (kVec) {
+    for (int32_t i = threadIdx.x; i < kFillBytes / 16; i += kThreads) sfill[i] = fv;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
   int32_t vend = c0;
   if constexpr (kVec) {
-    const int32_t ntiles = c1 > c0 ? (c1 - c0) / TILE : 0;
     vend = c0 + ntiles * TILE;
-    // the allow word of the next tile is loaded while this tile streams
-    uint32_t w_next = 0;
-    if (brow != nullptr && lane < WPT && warp < ntiles) w_next = __ldg(brow + ((c0 + warp * TILE) >> 5) + lane);
     for (int32_t ti = warp; ti < ntiles; ti += kWarps) {
+      const uint32_t w = (brow != nullptr && lane < WPT) ? sbits[ti * WPT + lane] : 0u;
+      const bool dead = !__any_sync(kAll, w != 0u);
+      if (lane == 0) sdead[ti] = dead ? 1 : 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      bool issued = false;
+      for (int32_t ti = 0; ti < ntiles;) {
+        if (!sdead[ti]) {
+          ++ti;
+          continue;
+        }
+        int32_t te = ti + 1;
+        while (te < ntiles && sdead[te]) ++te;
+        bulk_fill(row + c0 + ti * TILE, static_cast<uint32_t>((te - ti) * TILE * sizeof(T)), sfill);
+        if constexpr (kArgmax) arg_one(st, fill_key, c0 + ti * TILE);
+        issued = true;
+        ti = te;
+      }
+      if (issued) {
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+    }
+    for (int32_t ti = warp; ti < ntiles; ti += kWarps) {
+      if (sdead[ti]) continue;
       const int32_t tb = c0 + ti * TILE;
-      const uint32_t w = w_next;
-      if (brow != nullptr && lane < WPT && ti + kWarps < ntiles)
-        w_next = __ldg(brow + ((tb + kWarps * TILE) >> 5) + lane);
+      const uint32_t w = (brow != nullptr && lane < WPT) ? sbits[ti * WPT + lane] : 0u;
       uint32_t bits[kVPT];
 #pragma unroll
       for (int j = 0; j < kVPT; ++j) {
@@ -120,7 +200,7 @@ __device__ __forceinline__ void mask_range(T* __restrict__ row, int32_t c0, int3
         if (bits[j] == FULL) {
           if constexpr (kArgmax) arg_vec<T>(st, val[j], e0);
         } else if (bits[j] == 0u) {
-          __stcs(base + lane + 32 * j, vec_splat<T>(fill));
+          __stcs(base + lane + 32 * j, fv);
           if constexpr (kArgmax) arg_one(st, fill_key, e0);
         } else {
           const uint4 out = vec_blend<T>(val[j], bits[j], fill);
@@ -132,7 +212,7 @@ __device__ __forceinline__ void mask_range(T* __restrict__ row, int32_t c0, int3
   }
   Bits* rb = reinterpret_cast<Bits*>(row);
   for (int32_t e = vend + static_cast<int32_t>(threadIdx.x); e < c1; e += kThreads) {
-    const bool allowed = brow != nullptr && ((__ldg(brow + (e >> 5)) >> (e & 31)) & 1u);
+    const bool allowed = brow != nullptr && ((sbits[(e >> 5) - w0] >> (e & 31)) & 1u);
     if (allowed) {
       if constexpr (kArgmax) arg_one(st, order_key(Dt<T>::to_float(rb[e])), e);
     } else {
