@@ -33,6 +33,7 @@
 // Per mask call (all on the caller's stream, no host sync):
 //   memset(dedup) -> lookup_kernel -> claim_kernel -> compute_kernel -> apply.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "stream.cuh"
@@ -201,9 +202,9 @@ struct Memo {
   int32_t ws;       // words per allow row (multiple of 4)
 };
 
-size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+constexpr size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
-int32_t words_stride(int32_t vocab) { return ((((vocab + 31) / 32) + 3) / 4) * 4; }
+constexpr int32_t words_stride(int32_t vocab) { return ((((vocab + 31) / 32) + 3) / 4) * 4; }
 
 Memo memo_view(void* base, int32_t cap, int32_t vocab) {
   Memo m{};
@@ -241,7 +242,7 @@ struct Work {
   uint32_t* bits;    // [batch][ws] allow rows of representatives without a memo entry
 };
 
-int32_t pow2_at_least(int32_t x) {
+constexpr int32_t pow2_at_least(int32_t x) {
   int32_t p = 1;
   while (p < x) p <<= 1;
   return p;
@@ -267,8 +268,8 @@ Work work_view(void* base, int32_t batch, int32_t vocab) {
   return w;
 }
 
-size_t work_bytes(int32_t batch, int32_t vocab) {
-  const int32_t dcap = pow2_at_least(std::max(2 * batch, 2));
+constexpr size_t work_bytes(int32_t batch, int32_t vocab) {
+  const int32_t dcap = pow2_at_least(2 * batch > 2 ? 2 * batch : 2);
   return align256(sizeof(int32_t) * dcap) + 2 * align256(sizeof(int32_t) * batch) +
          align256(sizeof(uint64_t) * batch) + align256(sizeof(uint32_t) * 8 * batch) +
          align256(sizeof(int32_t) * batch) +
@@ -797,4 +798,67 @@ extern "C" bpd_status bpd_pda_is_complete(const bpd_pda_grammar* g, const int32_
   complete_kernel<<<(batch + 127) / 128, 128, 0, as_stream(stream)>>>(*g, config_pool, slots,
                                                                       broken, batch, complete_out);
   return check_launch("pda complete_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of bpd_pda_apply_mask (no counterpart in the
+// reference). Its per-call scratch lives in one fixed device array of this
+// library, sized for BPD_NOALLOC_MAX_BATCH rows of up to BPD_NOALLOC_MAX_VOCAB
+// tokens; every device that loads the library holds that array until exit.
+
+namespace bpd {
+namespace {
+
+constexpr size_t kNoAllocBytes = work_bytes(BPD_NOALLOC_MAX_BATCH, BPD_NOALLOC_MAX_VOCAB);
+constexpr int kMaxDevices = 64;
+
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// symbol itself is only a host-side stand-in, so the address is looked up
+// once per device (cudaGetSymbolAddress, with that device current) and cached.
+bpd_status noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(BPD_ERR_CAPACITY, "bpd_pda_apply_mask_noalloc: device %d beyond %d", dev,
+                kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(BPD_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return BPD_OK;
+}
+
+}  // namespace
+}  // namespace bpd
+
+extern "C" bpd_status bpd_pda_apply_mask_noalloc(const bpd_pda_grammar* g, void* logits,
+                                                 int32_t dtype, int64_t row_stride,
+                                                 const int32_t* config_pool, const int64_t* slots,
+                                                 const uint8_t* broken, int32_t batch, void* memo,
+                                                 int32_t memo_capacity, float neg_inf,
+                                                 void* stream) {
+  BPD_REQUIRE(batch >= 0, "bpd_pda_apply_mask_noalloc: bad batch");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(g != nullptr, "bpd_pda_apply_mask_noalloc: null grammar");
+  if (batch > BPD_NOALLOC_MAX_BATCH || g->vocab_size > BPD_NOALLOC_MAX_VOCAB)
+    return fail(BPD_ERR_CAPACITY,
+                "bpd_pda_apply_mask_noalloc: batch %d / vocab %d exceed the built-in scratch "
+                "(at most %d rows of %d tokens); use bpd_pda_apply_mask with a workspace",
+                batch, g->vocab_size, BPD_NOALLOC_MAX_BATCH, BPD_NOALLOC_MAX_VOCAB);
+  void* scratch = nullptr;
+  const bpd_status rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return bpd_pda_apply_mask(g, logits, dtype, row_stride, config_pool, slots, broken, batch,
+                            memo, memo_capacity, scratch, neg_inf, stream);
 }

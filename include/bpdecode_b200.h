@@ -215,6 +215,29 @@ bpd_status bpd_pda_advance(
     int32_t batch, const void* tokens, int32_t tokens_int64, uint8_t* ok_out,
     uint8_t* broken, int32_t* status_out, void* stream);
 
+/* Allocation-free form of bpd_pda_apply_mask, for callers that cannot
+ * allocate device memory at the point they mask: a serving engine that has
+ * handed (nearly) all of HBM to its own pool or KV cache, so a raw cudaMalloc
+ * would fail or fragment that pool, or a foreign-language binding (ctypes,
+ * FFI) that has no access to the host framework's allocator. No counterpart in
+ * the reference. Same arguments and results as bpd_pda_apply_mask minus the
+ * workspace: the per-call scratch is a fixed device array built into this
+ * library, sized for at most BPD_NOALLOC_MAX_BATCH rows of at most
+ * BPD_NOALLOC_MAX_VOCAB tokens (about 4.2 MB, held on every device that loads
+ * the library until exit); larger calls fail with BPD_ERR_CAPACITY. memo may
+ * be NULL (no mask caching). Nothing here calls cudaMalloc or cudaFree.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture. All calls share the one array, so calls that can overlap on the
+ * GPU (different streams, different host threads) race on it: serialise them
+ * on one stream. Each call clears what it needs zeroed itself. */
+#define BPD_NOALLOC_MAX_BATCH 128
+#define BPD_NOALLOC_MAX_VOCAB 262144
+bpd_status bpd_pda_apply_mask_noalloc(
+    const bpd_pda_grammar* g, void* logits, int32_t dtype, int64_t row_stride,
+    const int32_t* config_pool, const int64_t* slots, const uint8_t* broken,
+    int32_t batch, void* memo, int32_t memo_capacity, float neg_inf, void* stream);
+
 /* complete_out[b] (uint8) = pda_is_complete(pool[slots[b]]) && !broken
  * (pda.hpp:238-244; CFGConstraintBatch.is_complete, grammar/device.py:286-297). */
 bpd_status bpd_pda_is_complete(
