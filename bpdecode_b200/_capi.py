@@ -62,6 +62,8 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
                                   _I32, _P, _F, _P]),
     "bpd_pda_apply_mask_noalloc": (_I32, [C.POINTER(PdaGrammar), _P, _I32, _I64, _P, _P, _P,
                                           _I32, _P, _I32, _F, _P]),
+    "bpd_pda_step_greedy": (_I32, [C.POINTER(PdaGrammar), _P, _I32, _I64, _P, _P, _P, _I32, _P,
+                                   _I32, _P, _F, _P, _P, _I32, _P]),
     "bpd_pda_advance": (_I32, [C.POINTER(PdaGrammar), _P, _P, _I32, _P, _I32, _P, _P, _P, _P]),
     "bpd_pda_is_complete": (_I32, [C.POINTER(PdaGrammar), _P, _P, _P, _I32, _P, _P]),
 }

@@ -1,4 +1,5 @@
 // Library-wide C ABI helpers: version string and per-thread error messages.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -22,6 +23,21 @@ bpd_status check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return BPD_OK;
+}
+
+int32_t sm_count() {
+  static std::atomic<int32_t> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int32_t n = cache[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    n = v;
+    cache[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
 }
 
 }  // namespace bpd

@@ -18,6 +18,9 @@ bpd_status fail(bpd_status code, const char* fmt, ...);
 // Checks the launch that was just enqueued.
 bpd_status check_launch(const char* what);
 
+// Multiprocessor count of the current device (cached per device).
+int32_t sm_count();
+
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

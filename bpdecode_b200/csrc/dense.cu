@@ -14,15 +14,11 @@
 //   mixed                 -> load, blend, store
 // so a typical grammar state (almost everything rejected) moves about one
 // write of the row instead of a read plus a write.
-#include <cooperative_groups.h>
-
 #include <algorithm>
 #include <climits>
 
 #include "common.cuh"
 #include "stream.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace bpd {
 namespace {
@@ -100,90 +96,37 @@ __device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__
   return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
 }
 
-// Register cap of the streaming kernels (resident CTAs per SM) and warp tiles
-// per warp of one apply CTA; tuned on B200.
-#ifndef BPD_APPLY_MIN_BLOCKS
-#define BPD_APPLY_MIN_BLOCKS 8
-#endif
-#ifndef BPD_APPLY_TILES_PER_WARP
-#define BPD_APPLY_TILES_PER_WARP 4
-#endif
-
-template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
-    dense_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V,
-                       const int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
-                       const uint32_t* __restrict__ bits, int32_t wstride, int32_t S,
-                       typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
-  const int32_t row = blockIdx.x / chunks_per_row;
-  const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
-  const int32_t c1 = min(V, c0 + chunk);
-  int32_t s;
-  const uint32_t* brow = state_row(pool, slots, row, bits, wstride, S, &s, nullptr);
-  extern __shared__ __align__(16) uint8_t smem[];
-  ArgState st;
-  mask_chunk<T, kVec, false>(logits + row * row_stride, c0, c1, brow, fill, st, smem);
-}
-
-// Minimum resident CTAs per SM the fused step is compiled for (register cap).
-#ifndef BPD_STEP_MIN_BLOCKS
-#define BPD_STEP_MIN_BLOCKS 8
-#endif
-
-// Fused greedy step. A thread-block cluster of `k` CTAs owns one row; every
-// CTA masks its slice and reduces its first-maximal element; the partials are
-// written into rank 0's shared memory (distributed shared memory), and after
-// one cluster barrier rank 0 commits the winning token.
-template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
-    dense_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V,
-                      int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
-                      const uint32_t* __restrict__ bits, int32_t wstride,
-                      const int32_t* __restrict__ tok_next, int32_t S, typename Dt<T>::Bits fill,
-                      int32_t chunk, int64_t* __restrict__ token_out,
-                      int32_t* __restrict__ next_out) {
-  __shared__ uint64_t warp_best[kWarps];
-  __shared__ uint64_t cluster_best[8];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int32_t k = static_cast<int32_t>(cluster.num_blocks());
-  const int32_t rank = static_cast<int32_t>(cluster.block_rank());
-  const int32_t row = blockIdx.x / k;
-  const int32_t c0 = rank * chunk;
-  const int32_t c1 = min(V, c0 + chunk);
-  int32_t s;
-  int64_t slot;
-  const uint32_t* brow = state_row(pool, slots, row, bits, wstride, S, &s, &slot);
-
-  extern __shared__ __align__(16) uint8_t smem[];
-  ArgState st;
-  mask_chunk<T, kVec, true>(logits + row * row_stride, c0, c1, brow, fill, st, smem);
-
-  uint64_t mine = pack_arg(st.key, st.idx);
-  mine = warp_max_u64(mine);
-  const int32_t lane = threadIdx.x & 31;
-  const int32_t warp = threadIdx.x >> 5;
-  if (lane == 0) warp_best[warp] = mine;
-  __syncthreads();
-  if (warp == 0) {
-    uint64_t q = lane < kWarps ? warp_best[lane] : 0;
-    q = warp_max_u64(q);
-    if (lane == 0) {
-      uint64_t* dst = cluster.map_shared_rank(cluster_best, 0);
-      dst[rank] = q;
-    }
+struct DenseRows {
+  const int32_t* pool;
+  const int64_t* slots;
+  const uint32_t* bits;
+  int32_t wstride;
+  int32_t S;
+  __device__ __forceinline__ RowInfo operator()(int32_t row) const {
+    RowInfo r;
+    r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);
+    return r;
   }
-  cluster.sync();
-  if (rank == 0 && threadIdx.x == 0) {
-    uint64_t best = 0;
-    for (int32_t r = 0; r < k; ++r) best = cluster_best[r] > best ? cluster_best[r] : best;
-    const int32_t tok = unpack_idx(best);
-    const int32_t next =
-        (s >= 0 && s < S && tok >= 0 && tok < V) ? tok_next[static_cast<int64_t>(s) * V + tok] : -1;
-    pool[slot] = next;
+};
+
+// Dense commit of the chosen token: next = tok_next[state, token] (ops.py:301-306).
+struct DenseCommit {
+  int32_t* pool;
+  const int32_t* tok_next;
+  int32_t S;
+  int32_t V;
+  int64_t* token_out;
+  int32_t* next_out;
+  __device__ __forceinline__ void operator()(int32_t row, const RowInfo& r, int32_t tok) const {
+    const int32_t s = r.state;
+    const int32_t next = (s >= 0 && s < S && tok >= 0 && tok < V)
+                             ? tok_next[static_cast<int64_t>(s) * V + tok]
+                             : -1;
+    pool[r.slot] = next;
     token_out[row] = tok;
     if (next_out) next_out[row] = next;
   }
-}
+};
 
 __global__ void dense_advance_kernel(int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
                                      int32_t B, const void* __restrict__ tokens, int32_t tokens64,
@@ -223,31 +166,9 @@ template <typename T>
 bpd_status launch_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
                         const int32_t* pool, const int64_t* slots, const uint32_t* bits,
                         int32_t wstride, int32_t S, float neg_inf, cudaStream_t st) {
-  constexpr int TILE = tile_elems<T>();
-  const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-  const int32_t chunk = TILE * kWarps * BPD_APPLY_TILES_PER_WARP;
-  const int32_t chunks = (V + chunk - 1) / chunk;
-  const int64_t grid = static_cast<int64_t>(batch) * chunks;
-  BPD_REQUIRE(grid < INT_MAX, "batch too large");
-  const auto fill = Dt<T>::from_float_host(neg_inf);
-  const size_t smem = stream_smem_bytes<T>(chunk);
-  T* lg = static_cast<T*>(logits);
-  if (vec) {
-    dense_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
-        lg, row_stride, V, pool, slots, bits, wstride, S, fill, chunk, chunks);
-  } else {
-    dense_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
-        lg, row_stride, V, pool, slots, bits, wstride, S, fill, chunk, chunks);
-  }
-  return check_launch("dense_apply_kernel");
-}
-
-int32_t auto_ctas_per_row(int32_t batch) {
-  // aim for ~1.5 waves of 8 resident CTAs on each of the 148 SMs
-  const int32_t want = (148 * 12 + batch - 1) / batch;
-  int32_t k = 1;
-  while (k < want && k < 8) k <<= 1;
-  return k;
+  return launch_stream_apply<T, DenseRows>(logits, row_stride, batch, V,
+                                           DenseRows{pool, slots, bits, wstride, S}, neg_inf, st,
+                                           "dense apply kernel");
 }
 
 template <typename T>
@@ -255,38 +176,9 @@ bpd_status launch_step(void* logits, int64_t row_stride, int32_t batch, int32_t 
                        const int64_t* slots, const uint32_t* bits, int32_t wstride,
                        const int32_t* tok_next, int32_t S, float neg_inf, int64_t* token_out,
                        int32_t* next_out, int32_t k, cudaStream_t st) {
-  constexpr int TILE = tile_elems<T>();
-  const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-  const int32_t per = (V + k - 1) / k;
-  const int32_t chunk = ((per + TILE - 1) / TILE) * TILE;
-  const int64_t grid = static_cast<int64_t>(batch) * k;
-  BPD_REQUIRE(grid < INT_MAX, "batch too large");
-  const auto fill = Dt<T>::from_float_host(neg_inf);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = stream_smem_bytes<T>(chunk);
-  BPD_REQUIRE(cfg.dynamicSmemBytes <= 48 * 1024,
-              "bpd_dense_step_greedy: vocab too large for %d CTAs per row", k);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(k);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  T* lg = static_cast<T*>(logits);
-  cudaError_t e;
-  if (vec) {
-    e = cudaLaunchKernelEx(&cfg, dense_step_kernel<T, true>, lg, row_stride, V, pool, slots, bits,
-                           wstride, tok_next, S, fill, chunk, token_out, next_out);
-  } else {
-    e = cudaLaunchKernelEx(&cfg, dense_step_kernel<T, false>, lg, row_stride, V, pool, slots, bits,
-                           wstride, tok_next, S, fill, chunk, token_out, next_out);
-  }
-  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "dense_step_kernel: %s", cudaGetErrorString(e));
-  return check_launch("dense_step_kernel");
+  return launch_stream_step<T, DenseRows, DenseCommit>(
+      logits, row_stride, batch, V, DenseRows{pool, slots, bits, wstride, S},
+      DenseCommit{pool, tok_next, S, V, token_out, next_out}, neg_inf, k, st, "dense step kernel");
 }
 
 }  // namespace

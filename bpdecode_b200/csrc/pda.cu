@@ -31,7 +31,9 @@
 //   like the dense path.
 //
 // Per mask call (all on the caller's stream, no host sync):
-//   memset(dedup) -> lookup_kernel -> claim_kernel -> compute_kernel -> apply.
+//   memset(dedup) -> lookup_kernel (memo probe, dedup, memo claim)
+//   -> first_byte_kernel -> compute_kernel (misses only; both exit at once when
+//   every row hit) -> apply, or the fused step (apply + argmax) -> advance.
 #include <algorithm>
 #include <mutex>
 
@@ -194,7 +196,9 @@ __device__ __forceinline__ void w_copy(int32_t* dst, const int32_t* src, int lan
 // Memo / workspace layout.
 
 struct Memo {
-  uint32_t* tag;    // [cap] 0 = empty, 1 = filled
+  uint32_t* epoch;  // [1] calls so far; entries claimed by the running call carry
+                    //     tag epoch + 1 and are skipped by its own lookups
+  uint32_t* tag;    // [cap] 0 = empty, else the claiming call's tag
   uint64_t* hash;   // [cap]
   int32_t* key;     // [cap][NCFG] canonical config-sets
   uint32_t* bits;   // [cap][ws] allow rows
@@ -212,6 +216,8 @@ Memo memo_view(void* base, int32_t cap, int32_t vocab) {
   m.ws = words_stride(vocab);
   if (!base) return m;
   char* p = static_cast<char*>(base);
+  m.epoch = reinterpret_cast<uint32_t*>(p);
+  p += 256;
   m.tag = reinterpret_cast<uint32_t*>(p);
   p += align256(sizeof(uint32_t) * cap);
   m.hash = reinterpret_cast<uint64_t*>(p);
@@ -223,7 +229,7 @@ Memo memo_view(void* base, int32_t cap, int32_t vocab) {
 }
 
 size_t memo_bytes(int32_t cap, int32_t vocab) {
-  return align256(sizeof(uint32_t) * cap) + align256(sizeof(uint64_t) * cap) +
+  return 256 + align256(sizeof(uint32_t) * cap) + align256(sizeof(uint64_t) * cap) +
          align256(sizeof(int32_t) * NCFG * static_cast<size_t>(cap)) +
          align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(cap));
 }
@@ -234,6 +240,9 @@ constexpr int32_t kBroken = 0, kHit = 1, kRep = 2, kAlias = 3;
 struct Work {
   int32_t* dedup;    // [dcap] row index + 1 of the representative, 0 = empty
   int32_t dcap;      // power of two >= 2 * batch
+  int32_t* counters; // [4] right after dedup (cleared with it): representatives,
+                     //     next compute item, next first-byte item
+  int32_t* reps;     // [batch] representative rows, in claim order
   int32_t* kind;     // [batch]
   int32_t* ref;      // [batch] memo entry (kHit, kRep with memo), rep row (kAlias), -1
   uint64_t* hash;    // [batch]
@@ -253,7 +262,10 @@ Work work_view(void* base, int32_t batch, int32_t vocab) {
   w.dcap = pow2_at_least(std::max(2 * batch, 2));
   char* p = static_cast<char*>(base);
   w.dedup = reinterpret_cast<int32_t*>(p);
-  p += align256(sizeof(int32_t) * w.dcap);
+  w.counters = w.dedup + w.dcap;
+  p += align256(sizeof(int32_t) * (w.dcap + 4));
+  w.reps = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * batch);
   w.kind = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * batch);
   w.ref = reinterpret_cast<int32_t*>(p);
@@ -270,7 +282,7 @@ Work work_view(void* base, int32_t batch, int32_t vocab) {
 
 constexpr size_t work_bytes(int32_t batch, int32_t vocab) {
   const int32_t dcap = pow2_at_least(2 * batch > 2 ? 2 * batch : 2);
-  return align256(sizeof(int32_t) * dcap) + 2 * align256(sizeof(int32_t) * batch) +
+  return align256(sizeof(int32_t) * (dcap + 4)) + 3 * align256(sizeof(int32_t) * batch) +
          align256(sizeof(uint64_t) * batch) + align256(sizeof(uint32_t) * 8 * batch) +
          align256(sizeof(int32_t) * batch) +
          align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(batch));
@@ -342,107 +354,114 @@ __device__ __forceinline__ int64_t slot_of(const int64_t* slots, int32_t b) {
 // ---------------------------------------------------------------------------
 // Mask pipeline.
 
-// One CTA per row: memo lookup and in-batch dedup (warp 0), then the
-// surviving-first-byte table of representatives (all warps).
-__global__ void __launch_bounds__(kThreads)
+constexpr int kLookupWarps = 4;
+
+// One warp per row: memo lookup and in-batch dedup. A row whose content is
+// neither in the memo nor already claimed by an equal row of this call
+// becomes a representative: it is appended to the representative list and
+// its first-byte table is cleared for first_byte_kernel.
+__global__ void __launch_bounds__(kLookupWarps * 32)
     lookup_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
                   const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
-                  Memo memo, Work w) {
-  __shared__ int32_t base[NCFG];
-  __shared__ int32_t scratch[kWarps][NCFG];
-  __shared__ int32_t s_kind;
-  const int32_t b = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+                  int32_t batch, Memo memo, Work w) {
+  const int lane = threadIdx.x & 31;
+  const int32_t b = blockIdx.x * kLookupWarps + (threadIdx.x >> 5);
+  if (b >= batch) return;
   const int64_t slot = slot_of(slots, b);
   if (broken && broken[slot]) {
-    if (threadIdx.x == 0) {
+    if (lane == 0) {
       w.kind[b] = kBroken;
       w.ref[b] = -1;
     }
     return;
   }
-  const int32_t* row = pool + slot * NCFG;
-  for (int k = threadIdx.x; k < NCFG; k += kThreads) base[k] = row[k];
-  __syncthreads();
-  if (warp == 0) {
-    const uint64_t h = w_hash(base, lane);
-    int32_t kind = kRep, ref = -1;
-    // memo (read-only in this kernel)
+  const int32_t* base = pool + slot * NCFG;
+  const uint64_t h = w_hash(base, lane);
+  int32_t kind = kRep, ref = -1;
+  uint32_t cur = 0;  // this call's tag
+  if (memo.cap) {
+    cur = *memo.epoch + 1u;
+    if (cur == 0u) cur = 1u;
+  }
+  // memo: entries claimed earlier in this call (tag == cur) are still being
+  // filled and are skipped; equal content claimed by this call is found
+  // through the in-batch dedup below instead
+  for (int p = 0; memo.cap && p < kProbe; ++p) {
+    const int32_t e = static_cast<int32_t>((h + p) & (memo.cap - 1));
+    const uint32_t tag = memo.tag[e];
+    if (tag == 0u) break;
+    if (tag == cur) continue;
+    if (memo.hash[e] == h && w_same(base, memo.key + static_cast<int64_t>(e) * NCFG, lane)) {
+      kind = kHit;
+      ref = e;
+      break;
+    }
+  }
+  if (kind != kHit) {
+    // in-batch dedup: the first row to claim a dedup slot for this content is
+    // the representative; equal rows become its aliases
+    for (int p = 0; p < w.dcap; ++p) {
+      const int32_t d = static_cast<int32_t>((h + p) & (w.dcap - 1));
+      int32_t prev = 0;
+      if (lane == 0) prev = atomicCAS(w.dedup + d, 0, b + 1);
+      prev = __shfl_sync(kAll, prev, 0);
+      if (prev == 0) break;  // representative
+      const int32_t other = prev - 1;
+      const int32_t* orow = pool + slot_of(slots, other) * NCFG;
+      if (w_same(base, orow, lane)) {
+        kind = kAlias;
+        ref = other;
+        break;
+      }
+    }
+  }
+  if (kind == kRep) {
+    if (lane < 8) w.first[static_cast<int64_t>(b) * 8 + lane] = 0u;
+    if (lane == 0) {
+      w.reps[atomicAdd(w.counters + 0, 1)] = b;
+      w.eos_ok[b] = is_complete(g, base) ? 1 : 0;
+    }
+    // claim a memo entry (none free along the probe: bits go to the workspace)
     for (int p = 0; memo.cap && p < kProbe; ++p) {
       const int32_t e = static_cast<int32_t>((h + p) & (memo.cap - 1));
-      if (memo.tag[e] == 0) break;
-      if (memo.hash[e] == h && w_same(base, memo.key + static_cast<int64_t>(e) * NCFG, lane)) {
-        kind = kHit;
+      uint32_t prev = 0;
+      if (lane == 0) prev = atomicCAS(memo.tag + e, 0u, cur);
+      prev = __shfl_sync(kAll, prev, 0);
+      if (prev == 0u) {
+        w_canonical(base, memo.key + static_cast<int64_t>(e) * NCFG, lane);
+        if (lane == 0) memo.hash[e] = h;
         ref = e;
         break;
       }
     }
-    if (kind != kHit) {
-      // in-batch dedup: the first row to claim a dedup slot for this content
-      // is the representative; equal rows become its aliases
-      for (int p = 0; p < w.dcap; ++p) {
-        const int32_t d = static_cast<int32_t>((h + p) & (w.dcap - 1));
-        int32_t prev = 0;
-        if (lane == 0) prev = atomicCAS(w.dedup + d, 0, b + 1);
-        prev = __shfl_sync(kAll, prev, 0);
-        if (prev == 0) break;  // representative
-        const int32_t other = prev - 1;
-        const int32_t* orow = pool + slot_of(slots, other) * NCFG;
-        if (w_same(base, orow, lane)) {
-          kind = kAlias;
-          ref = other;
-          break;
-        }
-      }
-    }
-    if (lane == 0) {
-      w.kind[b] = kind;
-      w.ref[b] = ref;
-      w.hash[b] = h;
-      s_kind = kind;
-    }
   }
-  __syncthreads();
-  if (s_kind != kRep) return;
-  // which first bytes keep the set alive: 32 bytes per warp
-  int32_t* tmp = scratch[warp];
-  uint32_t word = 0;
-  for (int j = 0; j < 32; ++j) {
-    const int byte = warp * 32 + j;
-    const bool ok = w_advance_byte<false>(g, base, tmp, byte, lane);
-    if (ok) word |= 1u << j;
+  if (lane == 0) {
+    w.kind[b] = kind;
+    w.ref[b] = ref;
+    w.hash[b] = h;
   }
-  if (lane == 0) w.first[static_cast<int64_t>(b) * 8 + warp] = word;
-  if (threadIdx.x == 0) w.eos_ok[b] = is_complete(g, base) ? 1 : 0;
 }
 
-// Representatives claim a memo entry (after every lookup of this call has
-// finished, so no lookup can observe a half-written entry).
-__global__ void claim_kernel(const int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
-                             int32_t batch, Memo memo, Work w) {
-  const int lane = threadIdx.x & 31;
-  const int32_t b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (b >= batch) return;
-  if (w.kind[b] != kRep) return;
-  if (memo.cap == 0) return;
-  const uint64_t h = w.hash[b];
-  int32_t got = -1;
-  for (int p = 0; p < kProbe; ++p) {
-    const int32_t e = static_cast<int32_t>((h + p) & (memo.cap - 1));
-    uint32_t prev = 0;
-    if (lane == 0) prev = atomicCAS(memo.tag + e, 0u, 1u);
-    prev = __shfl_sync(kAll, prev, 0);
-    if (prev == 0) {
-      got = e;
-      break;
-    }
-  }
-  if (got < 0) return;  // table full along this probe: bits go to the workspace
-  const int32_t* row = pool + slot_of(slots, b) * NCFG;
-  w_canonical(row, memo.key + static_cast<int64_t>(got) * NCFG, lane);
-  if (lane == 0) {
-    memo.hash[got] = h;
-    w.ref[b] = got;
+// Which first bytes keep each representative's set alive: one warp per
+// (representative, byte) item, items taken from a counter so the whole grid
+// works on however many representatives this call has (none: every warp
+// exits at once).
+__global__ void __launch_bounds__(kThreads)
+    first_byte_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
+                      const int64_t* __restrict__ slots, Work w) {
+  __shared__ int32_t scratch[kWarps][NCFG];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int32_t items = w.counters[0] * 256;
+  for (;;) {
+    int32_t item = 0;
+    if (lane == 0) item = atomicAdd(w.counters + 2, 1);
+    item = __shfl_sync(kAll, item, 0);
+    if (item >= items) break;
+    const int32_t b = w.reps[item >> 8];
+    const int byte = item & 255;
+    const int32_t* base = pool + slot_of(slots, b) * NCFG;
+    const bool ok = w_advance_byte<false>(g, base, scratch[warp], byte, lane);
+    if (ok && lane == 0) atomicOr(w.first + static_cast<int64_t>(b) * 8 + (byte >> 5), 1u << (byte & 31));
   }
 }
 
@@ -452,69 +471,85 @@ __device__ __forceinline__ uint32_t* rep_bits(const Memo& memo, const Work& w, i
   return w.bits + static_cast<int64_t>(b) * memo.ws;
 }
 
-// Allow bits of every representative row: a CTA owns `chunk` tokens of one
-// row; each warp decides 32 tokens at a time (lane = token), walking only the
-// ones whose first byte survives and that are longer than one byte.
+constexpr int32_t kComputeChunk = kWarps * 32 * 4;  // tokens per compute item
+
+// Allow bits of every representative row. Items are (representative, 1024
+// tokens) pairs taken from a counter by a resident grid; each warp decides 32
+// tokens at a time (lane = token), walking only the ones whose first byte
+// survives and that are longer than one byte.
 __global__ void __launch_bounds__(kThreads)
     compute_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
-                   const int64_t* __restrict__ slots, Memo memo, Work w, int32_t chunk,
-                   int32_t chunks_per_row) {
-  __shared__ int32_t base[NCFG];
+                   const int64_t* __restrict__ slots, Memo memo, Work w) {
   __shared__ int32_t buf[kWarps][2][NCFG];
   __shared__ uint32_t first[8];
-  const int32_t b = blockIdx.x / chunks_per_row;
-  if (w.kind[b] != kRep) return;
-  const int32_t c0 = (blockIdx.x - b * chunks_per_row) * chunk;
-  const int32_t V = g.vocab_size;
-  const int32_t c1 = min(V, c0 + chunk);
+  __shared__ int32_t s_item;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int32_t* row = pool + slot_of(slots, b) * NCFG;
-  for (int k = threadIdx.x; k < NCFG; k += kThreads) base[k] = row[k];
-  if (threadIdx.x < 8) first[threadIdx.x] = w.first[static_cast<int64_t>(b) * 8 + threadIdx.x];
-  __syncthreads();
-  const bool eos_ok = w.eos_ok[b] != 0;
-  const bool nonempty = n_of(base) > 0;
-  uint32_t* out = rep_bits(memo, w, b);
-  for (int32_t t0 = c0 + warp * 32; t0 < c1; t0 += kWarps * 32) {
-    const int32_t t = t0 + lane;
-    bool ok = false, walk = false;
-    int32_t o0 = 0, o1 = 0;
-    if (t < c1) {
-      if (t == g.eos_id) {
-        ok = eos_ok;
-      } else {
-        o0 = __ldg(g.tok_offsets + t);
-        o1 = __ldg(g.tok_offsets + t + 1);
-        if (o0 == o1) {
-          ok = nonempty;
+  const int32_t V = g.vocab_size;
+  const int32_t chunks = (V + kComputeChunk - 1) / kComputeChunk;
+  const int32_t items = w.counters[0] * chunks;
+  for (;;) {
+    __syncthreads();  // the previous item's shared state is no longer read
+    if (threadIdx.x == 0) s_item = atomicAdd(w.counters + 1, 1);
+    __syncthreads();
+    const int32_t item = s_item;
+    if (item >= items) break;
+    const int32_t b = w.reps[item / chunks];
+    const int32_t c0 = (item % chunks) * kComputeChunk;
+    const int32_t c1 = min(V, c0 + kComputeChunk);
+    const int32_t* base = pool + slot_of(slots, b) * NCFG;
+    if (threadIdx.x < 8) first[threadIdx.x] = w.first[static_cast<int64_t>(b) * 8 + threadIdx.x];
+    __syncthreads();
+    const bool eos_ok = w.eos_ok[b] != 0;
+    const bool nonempty = n_of(base) > 0;
+    uint32_t* out = rep_bits(memo, w, b);
+    for (int32_t t0 = c0 + warp * 32; t0 < c1; t0 += kWarps * 32) {
+      const int32_t t = t0 + lane;
+      bool ok = false, walk = false;
+      int32_t o0 = 0, o1 = 0;
+      if (t < c1) {
+        if (t == g.eos_id) {
+          ok = eos_ok;
         } else {
-          const int fb = __ldg(g.tok_bytes + o0);
-          if ((first[fb >> 5] >> (fb & 31)) & 1u) {
-            if (o1 - o0 == 1) ok = true;
-            else walk = true;
+          o0 = __ldg(g.tok_offsets + t);
+          o1 = __ldg(g.tok_offsets + t + 1);
+          if (o0 == o1) {
+            ok = nonempty;
+          } else {
+            const int fb = __ldg(g.tok_bytes + o0);
+            if ((first[fb >> 5] >> (fb & 31)) & 1u) {
+              if (o1 - o0 == 1) ok = true;
+              else walk = true;
+            }
           }
         }
       }
-    }
-    uint32_t todo = __ballot_sync(kAll, walk);
-    while (todo) {
-      const int j = __ffs(todo) - 1;
-      todo &= todo - 1;
-      const int32_t s = __shfl_sync(kAll, o0, j);
-      const int32_t e = __shfl_sync(kAll, o1, j);
-      const int32_t* cur = base;
-      int which = 0;
-      bool alive = true;
-      for (int32_t i = s; i < e && alive; ++i) {
-        int32_t* nxt = buf[warp][which];
-        alive = w_advance_byte<false>(g, cur, nxt, __ldg(g.tok_bytes + i), lane);
-        cur = nxt;
-        which ^= 1;
+      uint32_t todo = __ballot_sync(kAll, walk);
+      while (todo) {
+        const int j = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int32_t s = __shfl_sync(kAll, o0, j);
+        const int32_t e = __shfl_sync(kAll, o1, j);
+        const int32_t* cur = base;
+        int which = 0;
+        bool alive = true;
+        for (int32_t i = s; i < e && alive; ++i) {
+          int32_t* nxt = buf[warp][which];
+          alive = w_advance_byte<false>(g, cur, nxt, __ldg(g.tok_bytes + i), lane);
+          cur = nxt;
+          which ^= 1;
+        }
+        if (lane == j) ok = alive;
       }
-      if (lane == j) ok = alive;
+      const uint32_t word = __ballot_sync(kAll, ok);
+      if (lane == 0) out[t0 >> 5] = word;
     }
-    const uint32_t word = __ballot_sync(kAll, ok);
-    if (lane == 0) out[t0 >> 5] = word;
+  }
+  // the last kernel of every mask call: the next call gets a new tag (the
+  // lookups of this call, which read the old epoch, have all finished)
+  if (memo.cap && blockIdx.x == 0 && threadIdx.x == 0) {
+    uint32_t cur = *memo.epoch + 1u;
+    if (cur == 0u) cur = 1u;
+    *memo.epoch = cur;
   }
 }
 
@@ -526,18 +561,22 @@ __device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work
   return rep_bits(memo, w, rep);
 }
 
-template <typename T, bool kVec>
-__global__ void __launch_bounds__(kThreads, 8)
-    pda_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Memo memo, Work w,
-                     typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
-  const int32_t row = blockIdx.x / chunks_per_row;
-  const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
-  const int32_t c1 = min(V, c0 + chunk);
-  extern __shared__ __align__(16) uint8_t smem[];
-  ArgState st;
-  mask_chunk<T, kVec, false>(logits + row * row_stride, c0, c1, row_bits(memo, w, row), fill,
-                             st, smem);
-}
+// Row -> its allow words through the memo / workspace (nullptr for broken rows).
+struct PdaRows {
+  Memo memo;
+  Work w;
+  __device__ __forceinline__ RowInfo operator()(int32_t row) const {
+    return RowInfo{row_bits(memo, w, row), 0, 0};
+  }
+};
+
+// The fused PDA step's argmax only records the token; advance_kernel commits.
+struct TokenOut {
+  int64_t* token_out;
+  __device__ __forceinline__ void operator()(int32_t row, const RowInfo&, int32_t tok) const {
+    token_out[row] = tok;
+  }
+};
 
 __global__ void pda_bits_out_kernel(int32_t W, Memo memo, Work w, uint32_t* __restrict__ out) {
   const int32_t row = blockIdx.y;
@@ -645,20 +684,17 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
               "memo capacity must be a power of two");
   Memo memo = memo_view(memo_mem, cap, g->vocab_size);
   Work w = work_view(workspace, batch, g->vocab_size);
-  cudaError_t e = cudaMemsetAsync(w.dedup, 0, sizeof(int32_t) * w.dcap, st);
+  cudaError_t e = cudaMemsetAsync(w.dedup, 0, sizeof(int32_t) * (w.dcap + 4), st);
   if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memset dedup: %s", cudaGetErrorString(e));
-  lookup_kernel<<<batch, kThreads, 0, st>>>(*g, pool, slots, broken, memo, w);
+  lookup_kernel<<<(batch + kLookupWarps - 1) / kLookupWarps, kLookupWarps * 32, 0, st>>>(
+      *g, pool, slots, broken, batch, memo, w);
   rc = check_launch("pda lookup_kernel");
   if (rc) return rc;
-  claim_kernel<<<(batch * 32 + 127) / 128, 128, 0, st>>>(pool, slots, batch, memo, w);
-  rc = check_launch("pda claim_kernel");
+  const int32_t sms = sm_count();
+  first_byte_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, w);
+  rc = check_launch("pda first_byte_kernel");
   if (rc) return rc;
-  const int32_t chunk = kWarps * 32 * 16;  // 4096 tokens per CTA
-  const int32_t chunks = (g->vocab_size + chunk - 1) / chunk;
-  const int64_t grid = static_cast<int64_t>(batch) * chunks;
-  BPD_REQUIRE(grid < 0x7FFFFFFF, "batch too large");
-  compute_kernel<<<static_cast<unsigned>(grid), kThreads, 0, st>>>(*g, pool, slots, memo, w,
-                                                                   chunk, chunks);
+  compute_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, memo, w);
   rc = check_launch("pda compute_kernel");
   if (rc) return rc;
   *memo_out = memo;
@@ -669,23 +705,17 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
 template <typename T>
 bpd_status launch_pda_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
                             const Memo& memo, const Work& w, float neg_inf, cudaStream_t st) {
-  constexpr int TILE = tile_elems<T>();
-  const bool vec = aligned16(logits) && (row_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-  const int32_t chunk = TILE * kWarps * 4;
-  const int32_t chunks = (V + chunk - 1) / chunk;
-  const int64_t grid = static_cast<int64_t>(batch) * chunks;
-  BPD_REQUIRE(grid < 0x7FFFFFFF, "batch too large");
-  const auto fill = Dt<T>::from_float_host(neg_inf);
-  const size_t smem = stream_smem_bytes<T>(chunk);
-  T* lg = static_cast<T*>(logits);
-  if (vec) {
-    pda_apply_kernel<T, true><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
-        lg, row_stride, V, memo, w, fill, chunk, chunks);
-  } else {
-    pda_apply_kernel<T, false><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
-        lg, row_stride, V, memo, w, fill, chunk, chunks);
-  }
-  return check_launch("pda_apply_kernel");
+  return launch_stream_apply<T, PdaRows>(logits, row_stride, batch, V, PdaRows{memo, w}, neg_inf,
+                                         st, "pda apply kernel");
+}
+
+template <typename T>
+bpd_status launch_pda_step(void* logits, int64_t row_stride, int32_t batch, int32_t V,
+                           const Memo& memo, const Work& w, float neg_inf, int64_t* token_out,
+                           int32_t k, cudaStream_t st) {
+  return launch_stream_step<T, PdaRows, TokenOut>(logits, row_stride, batch, V, PdaRows{memo, w},
+                                                  TokenOut{token_out}, neg_inf, k, st,
+                                                  "pda step kernel");
 }
 
 }  // namespace
@@ -713,7 +743,8 @@ extern "C" bpd_status bpd_pda_memo_reset(void* memo, int32_t capacity, int32_t v
               "bpd_pda_memo_reset: capacity must be a power of two");
   BPD_REQUIRE(vocab_size > 0, "bpd_pda_memo_reset: bad vocab");
   Memo m = memo_view(memo, capacity, vocab_size);
-  const cudaError_t e = cudaMemsetAsync(m.tag, 0, sizeof(uint32_t) * capacity, as_stream(stream));
+  const cudaError_t e = cudaMemsetAsync(m.epoch, 0, 256 + sizeof(uint32_t) * capacity,
+                                        as_stream(stream));
   if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memo reset: %s", cudaGetErrorString(e));
   return BPD_OK;
 }
@@ -770,6 +801,47 @@ extern "C" bpd_status bpd_pda_apply_mask(const bpd_pda_grammar* g, void* logits,
     default:
       return fail(BPD_ERR_INVALID, "bpd_pda_apply_mask: unsupported logits dtype %d", dtype);
   }
+}
+
+extern "C" bpd_status bpd_pda_step_greedy(
+    const bpd_pda_grammar* g, void* logits, int32_t dtype, int64_t row_stride,
+    int32_t* config_pool, const int64_t* slots, uint8_t* broken, int32_t batch, void* memo,
+    int32_t memo_capacity, void* workspace, float neg_inf, int64_t* token_out,
+    int32_t* status_out, int32_t ctas_per_row, void* stream) {
+  BPD_REQUIRE(batch >= 0, "bpd_pda_step_greedy: bad batch");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(logits != nullptr && token_out != nullptr, "bpd_pda_step_greedy: null pointer");
+  BPD_REQUIRE(g && row_stride >= g->vocab_size, "bpd_pda_step_greedy: row_stride < vocab");
+  BPD_REQUIRE(ctas_per_row == 0 || ctas_per_row == 1 || ctas_per_row == 2 || ctas_per_row == 4 ||
+                  ctas_per_row == 8,
+              "bpd_pda_step_greedy: ctas_per_row must be 0, 1, 2, 4 or 8");
+  cudaStream_t st = as_stream(stream);
+  Memo m;
+  Work w;
+  bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
+                                    workspace, &m, &w, st);
+  if (rc) return rc;
+  const int32_t k = ctas_per_row ? ctas_per_row : auto_ctas_per_row(batch);
+  switch (dtype) {
+    case BPD_F32:
+      rc = launch_pda_step<float>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
+                                  token_out, k, st);
+      break;
+    case BPD_BF16:
+      rc = launch_pda_step<__nv_bfloat16>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
+                                          token_out, k, st);
+      break;
+    case BPD_F16:
+      rc = launch_pda_step<__half>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
+                                   token_out, k, st);
+      break;
+    default:
+      return fail(BPD_ERR_INVALID, "bpd_pda_step_greedy: unsupported logits dtype %d", dtype);
+  }
+  if (rc) return rc;
+  advance_kernel<<<(batch + kAdvWarps - 1) / kAdvWarps, kAdvWarps * 32, 0, st>>>(
+      *g, config_pool, slots, batch, token_out, 1, nullptr, broken, status_out);
+  return check_launch("pda advance_kernel");
 }
 
 extern "C" bpd_status bpd_pda_advance(const bpd_pda_grammar* g, int32_t* config_pool,

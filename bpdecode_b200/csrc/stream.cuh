@@ -10,6 +10,8 @@
 #include <climits>
 #include <type_traits>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace bpd {
@@ -220,6 +222,159 @@ __device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int3
       if constexpr (kArgmax) arg_one(st, fill_key, e);
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Kernels built on mask_chunk, shared by the dense and the PDA paths.
+
+// What a row masks against: its allow words (nullptr = reject everything) and,
+// for the dense commit, its state and pool slot.
+struct RowInfo {
+  const uint32_t* brow;
+  int32_t state;
+  int64_t slot;
+};
+
+// Register cap (resident CTAs per SM) and warp tiles per warp of one apply
+// CTA; tuned on B200 (8 resident CTAs beat fewer CTAs with more registers).
+#ifndef BPD_APPLY_MIN_BLOCKS
+#define BPD_APPLY_MIN_BLOCKS 8
+#endif
+#ifndef BPD_APPLY_TILES_PER_WARP
+#define BPD_APPLY_TILES_PER_WARP 4
+#endif
+#ifndef BPD_STEP_MIN_BLOCKS
+#define BPD_STEP_MIN_BLOCKS 8
+#endif
+
+// Mask only: one CTA per (row, segment); the hardware block scheduler hands
+// segments of cheap and expensive rows out dynamically.
+template <typename T, bool kVec, class Rows>
+__global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
+    stream_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
+                        typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
+  const int32_t row = blockIdx.x / chunks_per_row;
+  const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
+  const int32_t c1 = min(V, c0 + chunk);
+  const RowInfo info = rows(row);
+  extern __shared__ __align__(16) uint8_t smem[];
+  ArgState st;
+  mask_chunk<T, kVec, false>(logits + row * row_stride, c0, c1, info.brow, fill, st, smem);
+}
+
+// Fused greedy step: a thread-block cluster of `k` CTAs owns one row; every
+// CTA masks its slice and reduces its first-maximal element; the partials are
+// written into rank 0's shared memory (distributed shared memory), and after
+// one cluster barrier rank 0 hands the winning token to `commit`.
+template <typename T, bool kVec, class Rows, class Commit>
+__global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
+    stream_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
+                       Commit commit, typename Dt<T>::Bits fill, int32_t chunk) {
+  __shared__ uint64_t warp_best[kWarps];
+  __shared__ uint64_t cluster_best[8];
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int32_t k = static_cast<int32_t>(cluster.num_blocks());
+  const int32_t rank = static_cast<int32_t>(cluster.block_rank());
+  const int32_t row = blockIdx.x / k;
+  const int32_t c0 = rank * chunk;
+  const int32_t c1 = min(V, c0 + chunk);
+  const RowInfo info = rows(row);
+  extern __shared__ __align__(16) uint8_t smem[];
+  ArgState st;
+  mask_chunk<T, kVec, true>(logits + row * row_stride, c0, c1, info.brow, fill, st, smem);
+
+  const uint64_t mine = warp_max_u64(pack_arg(st.key, st.idx));
+  const int32_t lane = threadIdx.x & 31;
+  const int32_t warp = threadIdx.x >> 5;
+  if (lane == 0) warp_best[warp] = mine;
+  __syncthreads();
+  if (warp == 0) {
+    uint64_t q = lane < kWarps ? warp_best[lane] : 0;
+    q = warp_max_u64(q);
+    if (lane == 0) {
+      uint64_t* dst = cluster.map_shared_rank(cluster_best, 0);
+      dst[rank] = q;
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    uint64_t best = 0;
+    for (int32_t r = 0; r < k; ++r) best = cluster_best[r] > best ? cluster_best[r] : best;
+    commit(row, info, unpack_idx(best));
+  }
+}
+
+inline bool rows_aligned(const void* logits, int64_t row_stride, size_t esize) {
+  return aligned16(logits) && (row_stride * static_cast<int64_t>(esize)) % 16 == 0;
+}
+
+template <typename T, class Rows>
+bpd_status launch_stream_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
+                               const Rows& rows, float neg_inf, cudaStream_t st,
+                               const char* what) {
+  constexpr int TILE = tile_elems<T>();
+  const int32_t chunk = TILE * kWarps * BPD_APPLY_TILES_PER_WARP;
+  const int32_t chunks = (V + chunk - 1) / chunk;
+  const int64_t grid = static_cast<int64_t>(batch) * chunks;
+  if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
+  const auto fill = Dt<T>::from_float_host(neg_inf);
+  const size_t smem = stream_smem_bytes<T>(chunk);
+  T* lg = static_cast<T*>(logits);
+  if (rows_aligned(logits, row_stride, sizeof(T))) {
+    stream_apply_kernel<T, true, Rows><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
+        lg, row_stride, V, rows, fill, chunk, chunks);
+  } else {
+    stream_apply_kernel<T, false, Rows><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
+        lg, row_stride, V, rows, fill, chunk, chunks);
+  }
+  return check_launch(what);
+}
+
+// CTAs per row of the fused step when the caller leaves it to us: aim for
+// ~1.5 waves of 8 resident CTAs on each of the 148 SMs.
+inline int32_t auto_ctas_per_row(int32_t batch) {
+  const int32_t want = (148 * 12 + batch - 1) / batch;
+  int32_t k = 1;
+  while (k < want && k < 8) k <<= 1;
+  return k;
+}
+
+template <typename T, class Rows, class Commit>
+bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, int32_t V,
+                              const Rows& rows, const Commit& commit, float neg_inf, int32_t k,
+                              cudaStream_t st, const char* what) {
+  constexpr int TILE = tile_elems<T>();
+  const int32_t per = (V + k - 1) / k;
+  const int32_t chunk = ((per + TILE - 1) / TILE) * TILE;
+  const int64_t grid = static_cast<int64_t>(batch) * k;
+  if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
+  const auto fill = Dt<T>::from_float_host(neg_inf);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = stream_smem_bytes<T>(chunk);
+  if (cfg.dynamicSmemBytes > 48 * 1024)
+    return fail(BPD_ERR_INVALID, "%s: vocab too large for %d CTAs per row", what, k);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(k);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  T* lg = static_cast<T*>(logits);
+  cudaError_t e;
+  if (rows_aligned(logits, row_stride, sizeof(T))) {
+    e = cudaLaunchKernelEx(&cfg, stream_step_kernel<T, true, Rows, Commit>, lg, row_stride, V,
+                           rows, commit, fill, chunk);
+  } else {
+    e = cudaLaunchKernelEx(&cfg, stream_step_kernel<T, false, Rows, Commit>, lg, row_stride, V,
+                           rows, commit, fill, chunk);
+  }
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
 }
 
 }  // namespace bpd

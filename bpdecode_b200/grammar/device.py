@@ -399,6 +399,30 @@ class CFGConstraintBatch:
             self._broken.view(torch.uint8).data_ptr(), status.data_ptr(), _stream(status)))
         return status
 
+    def step_greedy(self, seq_ids: Sequence[Hashable], logits: torch.Tensor,
+                    neg_inf: float = float("-inf"), ctas_per_row: int = 0) -> torch.Tensor:
+        """NEW: ``apply_mask`` + ``logits.argmax(-1)`` + ``commit`` with the
+        argmax fused into the masking pass. Masks ``logits`` in place, commits
+        the first maximal token of every row and returns those tokens (int64);
+        the per-row commit status is kept in ``last_status``."""
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        if int(logits.shape[0]) != B:
+            raise RuntimeError("bpdecode_b200: one logits row per seq_id")
+        code = _check_logits(logits, self.g.vocab_size)
+        tokens = torch.empty(B, dtype=torch.int64, device=self.device)
+        status = torch.empty(B, dtype=torch.int32, device=self.device)
+        mbuf, cap = self.g.mask_memo()
+        ws = self.g.workspace(B)
+        L = _capi.lib()
+        L.check(L.bpd_pda_step_greedy(
+            C.byref(self.g._struct()), logits.data_ptr(), code, logits.stride(0),
+            self._configs.data_ptr(), slots.data_ptr(), self._broken.view(torch.uint8).data_ptr(),
+            B, mbuf.data_ptr(), cap, ws.data_ptr(), float(neg_inf), tokens.data_ptr(),
+            status.data_ptr(), int(ctas_per_row), _stream(logits)))
+        self.last_status = status
+        return tokens
+
     # --- queries ------------------------------------------------------
     def is_complete(self, seq_id: Hashable) -> bool:
         """True when the string so far is a full match (EOS is allowed)."""

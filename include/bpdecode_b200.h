@@ -203,6 +203,18 @@ bpd_status bpd_pda_apply_mask(
     int32_t batch, void* memo, int32_t memo_capacity, void* workspace,
     float neg_inf, void* stream);
 
+/* NEW fused greedy step of the PDA path: bpd_pda_apply_mask, then the first
+ * maximal token of every masked row (torch.argmax order) into token_out
+ * (int64 [batch]), then bpd_pda_advance of those tokens (broken / status_out
+ * as there; broken may be NULL). Identical results to apply_mask + argmax +
+ * commit (grammar/device.py:252-283) with one pass over the logits fewer.
+ * ctas_per_row as in bpd_dense_step_greedy. */
+bpd_status bpd_pda_step_greedy(
+    const bpd_pda_grammar* g, void* logits, int32_t dtype, int64_t row_stride,
+    int32_t* config_pool, const int64_t* slots, uint8_t* broken, int32_t batch,
+    void* memo, int32_t memo_capacity, void* workspace, float neg_inf,
+    int64_t* token_out, int32_t* status_out, int32_t ctas_per_row, void* stream);
+
 /* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64).
  * ok_out[b] (uint8, may be NULL) = 1 if the token was accepted; a rejected
  * token leaves the config-set unchanged; EOS sets ok = complete and never

@@ -232,3 +232,37 @@ def test_config4_workload_matches_oracle(orc: Oracle) -> None:
             c = before[r:r + 1].copy()
             orc.pda_advance(h, c, tok[r:r + 1].cpu().numpy())
             assert np.array_equal(batch._configs[r].cpu().numpy(), c[0]), (step, r)
+
+
+@pytest.mark.parametrize("name", ["paren", "pairs", "jsonvalue_v4096", "schema_v4096"])
+def test_fused_step_equals_unfused(name: str) -> None:
+    """step_greedy == apply_mask + argmax + commit: masked logits, tokens,
+    config rows, broken flags and status, over a few steps with a broken row
+    and bf16 logits."""
+    from bpdecode_b200.grammar.device import CFGConstraintBatch
+
+    g = _dev(name)
+    B = 24
+    a = CFGConstraintBatch(g, capacity=B)
+    b = CFGConstraintBatch(g, capacity=B)
+    ids = list(range(B))
+    for i in ids:
+        a.add(i)
+        b.add(i)
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    for step in range(8):
+        logits = torch.randn(B, g.vocab_size, generator=gen, device="cuda")
+        if step == 3:
+            logits[5] = float("-inf")  # an all -inf row picks token 0
+        if step % 2:
+            logits = logits.to(torch.bfloat16)
+        la, lb = logits.clone(), logits.clone()
+        a.apply_mask(ids, la)
+        tok = la.argmax(-1)
+        st = a.commit(ids, tok)
+        tb = b.step_greedy(ids, lb, ctas_per_row=(1, 2, 4, 8)[step % 4])
+        assert torch.equal(la, lb)
+        assert torch.equal(tb, tok)
+        assert torch.equal(b.last_status, st)
+        assert torch.equal(a._configs, b._configs)
+        assert torch.equal(a._broken, b._broken)
