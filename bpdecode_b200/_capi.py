@@ -50,6 +50,12 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "bpd_dense_mask_bits": (_I32, [_P, _P, _I32, _P, _I32, _I32, _I32, _P, _P]),
     "bpd_dense_step_greedy": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _F,
                                      _P, _P, _I32, _P]),
+    "bpd_walk_apply_mask": (_I32, [_P, _I32, _I64, _I32, _P, _I32, _I32, _P, _P, _I32, _P, _P,
+                                   _I32, _I32, _P, _F, _P]),
+    "bpd_walk_mask_bits": (_I32, [_P, _I32, _I32, _P, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _P,
+                                  _P]),
+    "bpd_walk_advance": (_I32, [_P, _I32, _I32, _P, _P, _I32, _P, _P, _I32, _I32, _P, _P, _I32,
+                                _I32, _P, _P]),
     "bpd_soft_workspace_bytes": (_S, [_I32]),
     "bpd_soft_build_lookahead": (_I32, [_P, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _P]),
     "bpd_soft_apply": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _I32, _F, _P]),

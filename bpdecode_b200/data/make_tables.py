@@ -28,6 +28,14 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "grammars.npz")
 
+# The JSON Schema of the reference's HF processor test (tests/test_grammar_hf.py:49-55).
+HF_SCHEMA = {
+    "type": "object",
+    "properties": {"name": {"enum": ["a", "b"]}, "age": {"enum": [0, 1, 2]}},
+    "required": ["name", "age"],
+    "additionalProperties": False,
+}
+
 # Small grammars the reference's own PDA tests use (tests/test_pda_device.py:30-34).
 PDA_TEST_GRAMMARS = {
     "paren": 'root ::= "(" root ")" | "x" | "y"',
@@ -86,6 +94,7 @@ def main() -> None:
     _pda_arrays("pda/jsonvalue",
                 CompiledGrammar.build(parse_gbnf(_PRIMITIVES + "\nroot ::= json-value\n")), out)
     _pda_arrays("pda/schema", schema_cg, out)
+    _pda_arrays("pda/hf_object", CompiledGrammar.build(json_schema_to_grammar(HF_SCHEMA)), out)
     for name, src in PDA_TEST_GRAMMARS.items():
         _pda_arrays(f"pda/{name}", CompiledGrammar.build(parse_gbnf(src)), out)
 

@@ -14,9 +14,10 @@ Differences from the reference, all additive:
   per token, 32x smaller than ``tok_next``), built on the device the first time
   a per-step op needs it. The mask kernels read these bits instead of
   gathering an int32 ``tok_next`` row per logit row.
-* a bundle without ``tok_next`` is densified on first use (B200's HBM holds
-  tables far past the reference's 32 M-entry auto-dense threshold, and the
-  per-step path is dense-only).
+* a bundle without ``tok_next`` runs the byte-walk kernels on the raw DFA, as
+  the reference's native ops do; :class:`~bpdecode_b200.batch.ConstraintBatch`
+  densifies its grammars on the device (B200's HBM holds tables far past the
+  reference's 32 M-entry auto-dense threshold).
 * :func:`step_greedy_` -- mask + argmax + commit fused into one launch.
 """
 
@@ -138,6 +139,10 @@ class FsaTensors:
         """Return a copy carrying the ``k``-step soft-lookahead bias table."""
         base = self.densify()
         return replace(base, lookahead=build_lookahead(base, k))
+
+    def _memo_empty_symbols(self) -> torch.Tensor:
+        # a vocabulary of empty tokens has no symbols; kernels still need a pointer
+        return torch.zeros(1, dtype=torch.int32, device=self.device)
 
     def dense_tables(self) -> tuple[torch.Tensor, torch.Tensor]:
         """(tok_next, allow_bits) on this bundle's CUDA device, built on first use
@@ -359,11 +364,16 @@ def apply_mask_(
     """In place: every disallowed logit of ``logits`` [batch, vocab] becomes
     ``neg_inf``, one grammar state per row; rows with a negative state (BROKEN /
     FREE) are fully masked (ops.py:262-281)."""
-    tok_next, bits = fsa.dense_tables()
     B = int(logits.shape[0])
     code = _check_logits(logits, fsa.vocab_size)
     st = _as_i32(states, B, fsa.device)
     L = _capi.lib()
+    if fsa.tok_next is None:
+        L.check(L.bpd_walk_apply_mask(
+            logits.data_ptr(), code, logits.stride(0), B, *_walk_args(fsa), st.data_ptr(),
+            float(neg_inf), _stream(logits)))
+        return logits
+    tok_next, bits = fsa.dense_tables()
     L.check(L.bpd_dense_apply_mask(
         logits.data_ptr(), code, logits.stride(0), B, fsa.vocab_size, st.data_ptr(), None,
         bits.data_ptr(), bits.shape[1], fsa.num_states, float(neg_inf), _stream(logits)))
@@ -373,12 +383,16 @@ def apply_mask_(
 def compute_mask(fsa: FsaTensors, states: torch.Tensor) -> torch.Tensor:
     """Packed allow-mask, uint32 bits in an int32 tensor [batch, ceil(vocab/32)]
     (LSB first), one state per row (ops.py:284-292)."""
-    _, bits = fsa.dense_tables()
     B = int(states.numel())
     st = _as_i32(states, B, fsa.device)
     W = (fsa.vocab_size + 31) // 32
     out = torch.empty((B, W), dtype=torch.int32, device=fsa.device)
     L = _capi.lib()
+    if fsa.tok_next is None:
+        L.check(L.bpd_walk_mask_bits(*_walk_args(fsa), st.data_ptr(), B, out.data_ptr(),
+                                     _stream(out)))
+        return out
+    _, bits = fsa.dense_tables()
     L.check(L.bpd_dense_mask_bits(st.data_ptr(), None, B, bits.data_ptr(), bits.shape[1],
                                   fsa.num_states, fsa.vocab_size, out.data_ptr(), _stream(out)))
     return out
@@ -387,16 +401,34 @@ def compute_mask(fsa: FsaTensors, states: torch.Tensor) -> torch.Tensor:
 def advance_state(fsa: FsaTensors, states: torch.Tensor, token_ids: torch.Tensor) -> torch.Tensor:
     """Next state per row after emitting ``token_ids``; ``-1`` if the token was
     off a valid path or the row was already broken (ops.py:295-310)."""
-    tok_next, _ = fsa.dense_tables()
     B = int(states.numel())
     st = _as_i32(states, B, fsa.device)
     tk = _tokens(token_ids, B, fsa.device)
     out = torch.empty(B, dtype=torch.int32, device=fsa.device)
     L = _capi.lib()
+    if fsa.tok_next is None:
+        L.check(L.bpd_walk_advance(*_walk_args(fsa), st.data_ptr(), tk.data_ptr(),
+                                   int(tk.dtype == torch.int64), B, out.data_ptr(),
+                                   _stream(out)))
+        return out
+    tok_next, _ = fsa.dense_tables()
     L.check(L.bpd_dense_advance(st.data_ptr(), None, B, tk.data_ptr(),
                                 int(tk.dtype == torch.int64), tok_next.data_ptr(),
                                 fsa.num_states, fsa.vocab_size, out.data_ptr(), 0, _stream(out)))
     return out
+
+
+def _walk_args(fsa: FsaTensors) -> tuple:
+    """(trans, S, M, accept, live, dead, offsets, symbols, V, eos) pointers of
+    the byte-walk entry points; the tensors must already be contiguous int32 /
+    uint8 on the device (FsaTensors keeps them so)."""
+    _require_cuda(fsa.trans, "FsaTensors")
+    sym = fsa.symbols
+    if sym.numel() == 0:
+        sym = fsa._memo_empty_symbols()
+    return (fsa.trans.data_ptr(), fsa.num_states, fsa.num_symbols, fsa.accept.data_ptr(),
+            fsa.live.data_ptr(), fsa.dead, fsa.offsets.data_ptr(), sym.data_ptr(),
+            fsa.vocab_size, fsa.eos_id)
 
 
 def _tokens(token_ids: torch.Tensor, n: int, device: torch.device) -> torch.Tensor:

@@ -123,6 +123,42 @@ bpd_status bpd_dense_step_greedy(
     int32_t ctas_per_row, void* stream);
 
 /* --------------------------------------------------------------------------
+ * Byte-walk path: the same ops on the raw symbol-class DFA, for automata
+ * that are not densified (no tok_next table). trans int32 [num_states *
+ * num_symbols], accept / live uint8 [num_states], tok_offsets int32 [vocab+1],
+ * tok_symbols int32 [tok_offsets[vocab]]; states int32 [batch]. Semantics of
+ * mask_cpu.cpp:51-81 (step / compute_mask).
+ * ------------------------------------------------------------------------ */
+
+/* In place: logits[b, t] = neg_inf where step(states[b], t) == -1. Replaces
+ * the apply_mask_ op's device path (bindings/torch_ops.cpp:109-152,
+ * mask_cuda.cu:123-139). batch <= 65535. */
+bpd_status bpd_walk_apply_mask(
+    void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
+    const int32_t* trans, int32_t num_states, int32_t num_symbols,
+    const uint8_t* accept, const uint8_t* live, int32_t dead,
+    const int32_t* tok_offsets, const int32_t* tok_symbols, int32_t vocab_size,
+    int32_t eos_id, const int32_t* states, float neg_inf, void* stream);
+
+/* Packed allow bits int32 [batch, ceil(vocab/32)] (the compute_mask op,
+ * bindings/torch_ops.cpp:154-189, mask_cuda.cu:53-80). batch <= 65535. */
+bpd_status bpd_walk_mask_bits(
+    const int32_t* trans, int32_t num_states, int32_t num_symbols,
+    const uint8_t* accept, const uint8_t* live, int32_t dead,
+    const int32_t* tok_offsets, const int32_t* tok_symbols, int32_t vocab_size,
+    int32_t eos_id, const int32_t* states, int32_t batch, uint32_t* out_bits,
+    void* stream);
+
+/* next_out[b] = step(states[b], tokens[b]) (the advance_state op,
+ * bindings/torch_ops.cpp:191-229, mask_cuda.cu:106-119). */
+bpd_status bpd_walk_advance(
+    const int32_t* trans, int32_t num_states, int32_t num_symbols,
+    const uint8_t* accept, const uint8_t* live, int32_t dead,
+    const int32_t* tok_offsets, const int32_t* tok_symbols, int32_t vocab_size,
+    int32_t eos_id, const int32_t* states, const void* tokens, int32_t tokens_int64,
+    int32_t batch, int32_t* next_out, void* stream);
+
+/* --------------------------------------------------------------------------
  * Soft lookahead (k-step backward sum-product bias)
  * ------------------------------------------------------------------------ */
 
