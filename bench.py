@@ -42,10 +42,9 @@ ALGO_BYTES_PER_ROW_STEP = 2 * V * E + 4 * ((V + 31) // 32) + 16
 
 
 def _dist() -> tuple[int, int, int]:
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return rank, world, local
+    from bpdecode_b200.shard import dist_info
+
+    return dist_info()
 
 
 def _peaks() -> tuple[float, str]:
@@ -261,16 +260,12 @@ def main() -> None:
         run_reference(args)
         return
 
+    from bpdecode_b200 import shard
+
     rank, world, local = _dist()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=device)
+    shard.init("nccl", device)
 
     vocab, fsas, pats = build_workload(rank, device)
     batch = make_batch(fsas, pats)
@@ -280,11 +275,7 @@ def main() -> None:
     bufs = [gen_logits(rank, i, device) for i in range(ring)]
     torch.cuda.synchronize()
 
-    def barrier() -> None:
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier()
+    barrier = shard.barrier
 
     # warm-up
     for i in range(args.warmup):
@@ -309,12 +300,7 @@ def main() -> None:
     barrier()
     elapsed_ms = t_all0.elapsed_time(t_all1)
     kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([elapsed_ms, kern_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms, kern_ms = float(t[0]), float(t[1])
+    elapsed_ms, kern_ms = shard.max_over_ranks([elapsed_ms, kern_ms], device)
 
     total_rows = ROWS_PER_GPU * world * args.steps
     value = total_rows / (elapsed_ms / 1000.0)
@@ -385,11 +371,7 @@ def main() -> None:
         line["cpu_baseline"] = cpu_baseline(torch.cat(tns), starts, pats, 256, 320)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-        dist.destroy_process_group()
+    shard.finish()
 
 
 def _pda_config4(device: torch.device, rank: int, steps: int = 256) -> dict:
@@ -549,6 +531,8 @@ def _reference_torch_gpu(batch, bufs, ring, device) -> dict:
 
 
 def _e2e(batch, ids, rank, device, steps, world) -> dict:
+    from bpdecode_b200 import shard
+
     """Same step through the public API from pinned host logits: every step
     copies its logits host -> device, runs ConstraintBatch.step_greedy and
     reads the chosen tokens back."""
@@ -560,10 +544,7 @@ def _e2e(batch, ids, rank, device, steps, world) -> dict:
         dev.copy_(host[i % nhost], non_blocking=True)
         out.copy_(batch.step_greedy(ids, dev), non_blocking=True)
     torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
+    shard.barrier()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record()
@@ -572,13 +553,7 @@ def _e2e(batch, ids, rank, device, steps, world) -> dict:
         out.copy_(batch.step_greedy(ids, dev), non_blocking=True)
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b)
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t[0])
+    ms = shard.max_over_ranks([a.elapsed_time(b)], device)[0]
     return {"value": ROWS_PER_GPU * world * steps / (ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": ROWS_PER_GPU * V * 2, "d2h_bytes_per_step": ROWS_PER_GPU * 8,
             "steps": steps, "ms_per_step": ms / steps,

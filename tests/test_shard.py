@@ -1,0 +1,56 @@
+"""Multi-process host logic of the sharded step (gloo, world size 2, CPU)."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import torch
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out) -> None:
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from bpdecode_b200 import shard
+    from bpdecode_b200.workloads import row_patterns
+
+    assert shard.init("gloo", timeout_s=60)
+    rows = shard.shard_rows(10, world, rank)
+    # per-rank work is independent: each rank draws its own rows' grammars
+    pats = row_patterns(len(rows), seed=rank)
+    elapsed = [1.5 + rank, 10.0 * rank]
+    mx = shard.max_over_ranks(elapsed)
+    tot = shard.sum_over_ranks([float(len(rows))])
+    shard.barrier()
+    out.put((rank, list(rows), len(pats), mx, tot))
+    shard.finish()
+
+
+def test_two_ranks_shard_rows_and_reduce_timings() -> None:
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    mp.start_processes(_worker, args=(world, _free_port(), q), nprocs=world, join=True,
+                       start_method="spawn")
+    got = sorted(q.get() for _ in range(world))
+    assert got[0][1] == [0, 1, 2, 3, 4] and got[1][1] == [5, 6, 7, 8, 9]
+    for _, _, n, mx, tot in got:
+        assert n == 5
+        assert mx == [2.5, 10.0]  # max over ranks of every entry
+        assert tot == [10.0]
+
+
+def test_single_process_is_identity() -> None:
+    from bpdecode_b200 import shard
+
+    assert shard.shard_rows(7, 1, 0) == range(0, 7)
+    assert shard.shard_rows(7, 3, 2) == range(5, 7)
+    assert shard.max_over_ranks([1.0, 2.0]) == [1.0, 2.0]
+    assert torch.distributed.is_available()
