@@ -33,6 +33,10 @@ if ROOT not in sys.path:
 V = 128_256
 ROWS_PER_GPU = 1024
 SIGMA = 2.0
+# Config 2 generates 128 steps per request: the timed run is a sequence of
+# such episodes, every row restarting from its pattern's start state each
+# EPISODE steps (ConstraintBatch.reset_many, one device write).
+EPISODE = 128
 METRIC = "constrained row-steps/sec (mask+apply+commit)"
 UNIT = "row-steps/s"
 # Algorithmic bytes of one row-step (bf16 logits, V = 128,256): logits read +
@@ -169,8 +173,11 @@ def cpu_baseline(tok_next_cpu: torch.Tensor, starts: list[int], pats: list[int],
     samples = [(torch.randn(rows, V, generator=g) * SIGMA).to(torch.bfloat16)
                for _ in range(min(steps, 4))]
     torch_port.step(samples[0], tok_next_cpu, state.clone(), slots)  # warm
+    start = state.clone()
     t0 = time.perf_counter()
     for i in range(steps):
+        if i and i % EPISODE == 0:
+            state.copy_(start)
         torch_port.step(samples[i % len(samples)], tok_next_cpu, state, slots)
     dt = time.perf_counter() - t0
     return {"value": rows * steps / dt, "unit": UNIT, "cores": torch.get_num_threads(),
@@ -209,10 +216,14 @@ def run_reference(args: argparse.Namespace) -> None:
     pool = [(torch.randn(rows, V, generator=g) * SIGMA).to(torch.bfloat16) for _ in range(4)]
     from oracle import torch_port
 
+    start = state.clone()
     for i in range(args.warmup):
         torch_port.step(pool[i % 4], tok_next, state, slots)
+    state.copy_(start)
     t0 = time.perf_counter()
     for i in range(args.steps):
+        if i and i % EPISODE == 0:
+            state.copy_(start)
         torch_port.step(pool[i % 4], tok_next, state, slots)
     dt = time.perf_counter() - t0
     value = rows * args.steps / dt
@@ -235,11 +246,70 @@ def run_reference(args: argparse.Namespace) -> None:
 def _config(world: int) -> dict:
     return {
         "workload": "dense regex step at serving scale: 8 regexes mixed per batch, "
-                    f"V={V}, {ROWS_PER_GPU} rows per GPU, bf16 logits N(0,{SIGMA:g}), argmax commit",
+                    f"V={V}, {ROWS_PER_GPU} rows per GPU, bf16 logits N(0,{SIGMA:g}), argmax "
+                    f"commit, {EPISODE}-step generations (BASELINE config 2)",
         "vocab": V, "rows_per_gpu": ROWS_PER_GPU, "global_batch": ROWS_PER_GPU * world,
         "parallelism": f"dp{world} (rows sharded by request, no collective)",
-        "l2": "inputs larger than L2: every step reads a fresh 262 MB logits buffer",
+        "l2": "inputs larger than L2: every step reads a 262 MB logits buffer (126 MB L2)",
     }
+
+
+def run_profile_case(args: argparse.Namespace) -> None:
+    """Small fixed cases for ncu captures (no timing, no side measurements):
+    `dense` = the bench's fused dense step (1024 rows, bf16, 8 logits buffers
+    of 262 MB, larger than L2); `pda` = the config-4 PDA step (256 rows,
+    fp32); `soft` = the fused soft-lookahead step (1024 rows, fp32, k = 4).
+    Each runs --warmup steps, restarts the rows (dense, soft), then --steps
+    steps on cuda:0."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    n = args.warmup + args.steps
+    ring = 8 if args.profile_case == "dense" else 4
+    if args.profile_case in ("dense", "soft"):
+        _, fsas, pats = build_workload(0, device)
+        if args.profile_case == "dense":
+            batch = make_batch(fsas, pats)
+            bufs = [gen_logits(0, i, device) for i in range(ring)]
+            step = batch.step_greedy
+        else:
+            from dataclasses import replace
+
+            from bpdecode_b200.ops import build_lookahead
+
+            soft = [replace(f, lookahead=build_lookahead(f, 4)) for f in fsas]
+            batch = make_batch(soft, pats)
+            bufs = [gen_logits(0, i, device).float() for i in range(ring)]
+
+            def step(ids, lg):
+                return batch.soft_step_greedy(ids, lg, 1.0)
+        ids = list(range(ROWS_PER_GPU))
+    else:
+        from bpdecode_b200 import tables
+        from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
+        from bpdecode_b200.workloads import BIASED, vocab_large
+
+        vocab = vocab_large(V)
+        g = PdaTensors.from_arrays(tables.load_pda("jsonvalue"), vocab, device)
+        batch = CFGConstraintBatch(g, capacity=256)
+        ids = list(range(256))
+        for i in ids:
+            batch.add(i)
+        bias = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
+        bufs = []
+        for i in range(ring):
+            gen = torch.Generator(device=device).manual_seed(40_000 + i)
+            x = torch.randn(256, V, generator=gen, device=device)
+            x[:, bias] += 3.0
+            bufs.append(x)
+        step = batch.step_greedy
+    for i in range(args.warmup):
+        step(ids, bufs[i % ring])
+    if args.profile_case != "pda":
+        batch.reset_many(ids)  # the captured steps start an episode, as in the bench
+    for i in range(args.steps):
+        step(ids, bufs[i % ring])
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "steps": n}), flush=True)
 
 
 def main() -> None:
@@ -253,9 +323,15 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the PDA and soft-lookahead side measurements")
+    ap.add_argument("--profile-case", choices=["dense", "pda", "soft"],
+                    help="run a few untimed steps of one hot kernel for an ncu capture "
+                         "(1 GPU, --warmup steps then --steps steps) and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.profile_case:
+        run_profile_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
         return
@@ -277,9 +353,10 @@ def main() -> None:
 
     barrier = shard.barrier
 
-    # warm-up
+    # warm-up, then every row back to its start state
     for i in range(args.warmup):
         batch.step_greedy(ids, bufs[i % ring])
+    batch.reset_many(ids)
     torch.cuda.synchronize()
     barrier()
 
@@ -292,8 +369,10 @@ def main() -> None:
         torch.cuda.synchronize()
         t_all0.record(stream)
         for i in range(args.steps):
+            if i and i % EPISODE == 0:
+                batch.reset_many(ids)
             ev[i][0].record(stream)
-            batch.step_greedy(ids, bufs[(args.warmup + i) % ring])
+            batch.step_greedy(ids, bufs[(i % EPISODE) % ring])
             ev[i][1].record(stream)
         t_all1.record(stream)
         torch.cuda.synchronize()
@@ -308,12 +387,14 @@ def main() -> None:
     achieved = ROWS_PER_GPU * ALGO_BYTES_PER_ROW_STEP / (kern_ms / 1000.0) / 1e9
     traffic = _profile_traffic()
 
-    # unfused drop-in path: apply_mask + torch.argmax + commit (3 launches)
+    # unfused drop-in path: apply_mask + torch.argmax + commit (3 launches),
+    # the first 64 steps of an episode
     un_steps = min(args.steps, 64)
     for i in range(3):
         lg = bufs[i % ring]
         batch.apply_mask(ids, lg)
         batch.commit(ids, lg.argmax(-1))
+    batch.reset_many(ids)
     torch.cuda.synchronize()
     u0 = torch.cuda.Event(enable_timing=True)
     u1 = torch.cuda.Event(enable_timing=True)
@@ -327,20 +408,23 @@ def main() -> None:
     un_ms = u0.elapsed_time(u1) / un_steps
 
     # reference GPU bar: bpdecode's dense torch composite on this B200
+    batch.reset_many(ids)
     ref_gpu = _reference_torch_gpu(batch, bufs, ring, device)
 
     # end to end through the public API with host buffers
+    batch.reset_many(ids)
     e2e = _e2e(batch, ids, rank, device, args.e2e_steps, world)
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {**_config(world), "logits_ring": ring,
-                   "ring_note": (f"{ring} pre-generated buffers; step i uses buffer i mod "
-                                 f"{ring}, so after {ring} steps a buffer is reused "
-                                 "(already masked in place)") if ring < args.steps else
-                   "every timed step reads its own fresh buffer"},
+        "config": {**_config(world), "logits_ring": ring, "episode_steps": EPISODE,
+                   "episodes": (args.steps + EPISODE - 1) // EPISODE,
+                   "ring_note": (f"every row restarts from its start state each {EPISODE} "
+                                 f"steps (one device write inside the timed region); step j "
+                                 f"of an episode reads buffer j mod {ring}, so every episode "
+                                 "replays the same trajectory (masking in place is idempotent)")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
@@ -458,7 +542,8 @@ def _pda_config4(device: torch.device, rank: int, steps: int = 256) -> dict:
 
 def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 64) -> dict:
     """Soft lookahead (horizon 4) over the 8-regex dense rows in fp32: table
-    build time, then apply_soft + argmax + commit per step."""
+    build time, then per step apply_soft + argmax + commit (the reference's
+    sequence) and the fused soft step (one launch)."""
     from dataclasses import replace
 
     from bpdecode_b200.batch import ConstraintBatch
@@ -468,33 +553,43 @@ def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 64
     soft = [replace(f, lookahead=build_lookahead(f, 4)) for f in fsas]
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
-    batch = ConstraintBatch(soft, capacity=ROWS_PER_GPU)
     ids = list(range(ROWS_PER_GPU))
-    for i in ids:
-        batch.add(i, grammar=pats[i])
     ring = min(steps, 16)
     bufs = [torch.randn(ROWS_PER_GPU, V, device=device,
                         generator=torch.Generator(device=device).manual_seed(rank * 31 + i))
             for i in range(ring)]
-    for i in range(3):
-        lg = bufs[i % ring]
+
+    def timed(step) -> float:
+        batch = ConstraintBatch(soft, capacity=ROWS_PER_GPU)
+        for i in ids:
+            batch.add(i, grammar=pats[i])
+        for i in range(3):
+            step(batch, bufs[i % ring])
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(steps):
+            step(batch, bufs[i % ring])
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    def unfused(batch, lg) -> None:
         batch.apply_soft(ids, lg, 1.0)
         batch.commit(ids, lg.argmax(-1))
-    torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for i in range(steps):
-        lg = bufs[i % ring]
-        batch.apply_soft(ids, lg, 1.0)
-        batch.commit(ids, lg.argmax(-1))
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / steps
-    return {"workload": f"soft lookahead k=4, 8 regexes, {ROWS_PER_GPU} rows, V={V}, fp32, "
-                        "apply_soft + argmax + commit",
-            "table_build_s": build_s, "ms_per_step": ms,
-            "row_steps_per_s": ROWS_PER_GPU / (ms / 1e3)}
+
+    ms = timed(unfused)
+    ms_fused = timed(lambda batch, lg: batch.soft_step_greedy(ids, lg, 1.0))
+    logit_bytes = 2 * 4 * V * ROWS_PER_GPU
+    return {"workload": f"soft lookahead k=4, 8 regexes, {ROWS_PER_GPU} rows, V={V}, fp32",
+            "table_build_s": build_s,
+            "unfused_ms_per_step": ms, "unfused_row_steps_per_s": ROWS_PER_GPU / (ms / 1e3),
+            "fused_ms_per_step": ms_fused,
+            "fused_row_steps_per_s": ROWS_PER_GPU / (ms_fused / 1e3),
+            "fused_logits_gbs": logit_bytes / (ms_fused / 1e3) / 1e9,
+            "note": "logits read + written once per step (2 x 4 B x V per row); "
+                    "lookahead rows (sum of states x V x 4 B) stay L2-resident"}
 
 
 def _reference_torch_gpu(batch, bufs, ring, device) -> dict:

@@ -58,7 +58,9 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
                                 _I32, _P, _P]),
     "bpd_soft_workspace_bytes": (_S, [_I32]),
     "bpd_soft_build_lookahead": (_I32, [_P, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _P]),
-    "bpd_soft_apply": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _I32, _F, _P]),
+    "bpd_soft_apply": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _P, _I32, _I32, _F, _P]),
+    "bpd_soft_step_greedy": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _P, _I32, _P, _I32,
+                                    _F, _P, _P, _I32, _P]),
     "bpd_pda_init": (_I32, [C.POINTER(PdaGrammar), _P, _P]),
     "bpd_pda_memo_bytes": (_S, [_I32, _I32]),
     "bpd_pda_memo_reset": (_I32, [_P, _I32, _I32, _P]),

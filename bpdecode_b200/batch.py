@@ -203,6 +203,21 @@ class ConstraintBatch:
     def reset(self, seq_id: Hashable) -> None:
         self._state[self._slot_of[seq_id]] = self._t.starts[self._grammar_of[seq_id]]
 
+    def reset_many(self, seq_ids: Sequence[Hashable]) -> None:
+        """NEW: :meth:`reset` of every id in ``seq_ids`` as one device write on
+        the current stream (no host synchronisation once the id list has been
+        seen, as with the per-step calls)."""
+        slots = self._slots(seq_ids)
+        key = ("starts",) + (seq_ids if isinstance(seq_ids, tuple) else tuple(seq_ids))
+        starts = self._slot_cache.get(key)
+        if starts is None:
+            starts = torch.tensor([self._t.starts[self._grammar_of[s]] for s in key[1:]],
+                                  dtype=torch.int32).to(self.device)
+            self._slot_cache[key] = starts
+            if len(self._slot_cache) > self._SLOT_CACHE:
+                self._slot_cache.popitem(last=False)
+        self._state.index_copy_(0, slots, starts)
+
     def __len__(self) -> int:
         return len(self._slot_of)
 
@@ -265,8 +280,8 @@ class ConstraintBatch:
         L = _capi.lib()
         L.check(L.bpd_soft_apply(
             logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
-            slots.data_ptr(), t.lookahead.data_ptr(), t.num_states, float(alpha),
-            _stream(logits)))
+            slots.data_ptr(), t.lookahead.data_ptr(), t.allow_bits.data_ptr(),
+            t.allow_bits.shape[1], t.num_states, float(alpha), _stream(logits)))
         return logits
 
     def commit(self, seq_ids: Sequence[Hashable], tokens: torch.Tensor) -> torch.Tensor:
@@ -307,6 +322,33 @@ class ConstraintBatch:
             slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1],
             t.tok_next.data_ptr(), t.num_states, float(neg_inf), tokens.data_ptr(), None,
             int(ctas_per_row), _stream(logits)))
+        return tokens
+
+    def soft_step_greedy(
+        self,
+        seq_ids: Sequence[Hashable],
+        logits: torch.Tensor,
+        alpha: float = 1.0,
+        ctas_per_row: int = 0,
+    ) -> torch.Tensor:
+        """NEW: ``apply_soft`` + ``logits.argmax(-1)`` + ``commit`` in one
+        launch. Biases ``logits`` in place and returns the chosen tokens
+        (int64, first maximal index)."""
+        t = self._t
+        if t.lookahead is None:
+            raise ValueError("fsa has no lookahead table; build with dense + with_lookahead")
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        if int(logits.shape[0]) != B:
+            raise RuntimeError("bpdecode_b200: one logits row per seq_id")
+        code = _check_logits(logits, t.vocab_size)
+        tokens = torch.empty(B, dtype=torch.int64, device=self.device)
+        L = _capi.lib()
+        L.check(L.bpd_soft_step_greedy(
+            logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
+            slots.data_ptr(), t.lookahead.data_ptr(), t.allow_bits.data_ptr(),
+            t.allow_bits.shape[1], t.tok_next.data_ptr(), t.num_states, float(alpha),
+            tokens.data_ptr(), None, int(ctas_per_row), _stream(logits)))
         return tokens
 
     # --- queries ------------------------------------------------------

@@ -122,13 +122,15 @@ __device__ __forceinline__ uint4 vec_blend(const uint4& v, uint32_t keep, typena
     return make_uint4((keep & 1) ? v.x : fill, (keep & 2) ? v.y : fill, (keep & 4) ? v.z : fill,
                       (keep & 8) ? v.w : fill);
   } else {
+    // the two bits of word k move to bits 0 and 16 (t + (t << 15) cannot carry
+    // for t < 256), and * 0xFFFF widens each to a 16-bit lane mask
     const uint32_t f2 = uint32_t(fill) | (uint32_t(fill) << 16);
-    auto mix = [&](uint32_t w, uint32_t two) -> uint32_t {
-      const uint32_t m = ((two & 1) ? 0x0000FFFFu : 0u) | ((two & 2) ? 0xFFFF0000u : 0u);
+    auto mix = [&](uint32_t w, uint32_t t) -> uint32_t {
+      const uint32_t m = ((t * 0x8001u) & 0x10001u) * 0xFFFFu;
       return (w & m) | (f2 & ~m);
     };
-    return make_uint4(mix(v.x, keep & 3), mix(v.y, (keep >> 2) & 3), mix(v.z, (keep >> 4) & 3),
-                      mix(v.w, (keep >> 6) & 3));
+    return make_uint4(mix(v.x, keep), mix(v.y, keep >> 2), mix(v.z, keep >> 4),
+                      mix(v.w, keep >> 6));
   }
 }
 

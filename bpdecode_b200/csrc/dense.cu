@@ -84,50 +84,6 @@ __global__ void build_allow_bits_kernel(const int32_t* __restrict__ tok_next, in
   if (w0 + lane < wstride) bits[static_cast<int64_t>(s) * wstride + w0 + lane] = mine;
 }
 
-__device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__ pool,
-                                                     const int64_t* __restrict__ slots,
-                                                     int32_t row, const uint32_t* __restrict__ bits,
-                                                     int32_t wstride, int32_t S, int32_t* state,
-                                                     int64_t* slot_out) {
-  const int64_t slot = slots ? slots[row] : row;
-  const int32_t s = pool[slot];
-  *state = s;
-  if (slot_out) *slot_out = slot;
-  return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
-}
-
-struct DenseRows {
-  const int32_t* pool;
-  const int64_t* slots;
-  const uint32_t* bits;
-  int32_t wstride;
-  int32_t S;
-  __device__ __forceinline__ RowInfo operator()(int32_t row) const {
-    RowInfo r;
-    r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);
-    return r;
-  }
-};
-
-// Dense commit of the chosen token: next = tok_next[state, token] (ops.py:301-306).
-struct DenseCommit {
-  int32_t* pool;
-  const int32_t* tok_next;
-  int32_t S;
-  int32_t V;
-  int64_t* token_out;
-  int32_t* next_out;
-  __device__ __forceinline__ void operator()(int32_t row, const RowInfo& r, int32_t tok) const {
-    const int32_t s = r.state;
-    const int32_t next = (s >= 0 && s < S && tok >= 0 && tok < V)
-                             ? tok_next[static_cast<int64_t>(s) * V + tok]
-                             : -1;
-    pool[r.slot] = next;
-    token_out[row] = tok;
-    if (next_out) next_out[row] = next;
-  }
-};
-
 __global__ void dense_advance_kernel(int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
                                      int32_t B, const void* __restrict__ tokens, int32_t tokens64,
                                      const int32_t* __restrict__ tok_next, int32_t S, int32_t V,

@@ -563,6 +563,7 @@ __device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work
 
 // Row -> its allow words through the memo / workspace (nullptr for broken rows).
 struct PdaRows {
+  static constexpr bool kSoft = false;
   Memo memo;
   Work w;
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {

@@ -17,11 +17,10 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "stream.cuh"
 
 namespace bpd {
 namespace {
-
-constexpr int kThreads = 256;
 
 __global__ void logz_init_kernel(const uint8_t* __restrict__ live, int32_t S, float* __restrict__ logz) {
   const int32_t s = blockIdx.x * blockDim.x + threadIdx.x;
@@ -106,42 +105,39 @@ __global__ void lookahead_out_kernel(const int32_t* __restrict__ tn, int32_t S, 
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-    soft_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V,
-                      const int32_t* __restrict__ pool, const int64_t* __restrict__ slots,
-                      const float* __restrict__ la, int32_t S, float alpha, int32_t chunk,
-                      int32_t chunks_per_row) {
-  using Bits = typename Dt<T>::Bits;
-  const int32_t row = blockIdx.x / chunks_per_row;
-  const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
-  const int32_t c1 = min(V, c0 + chunk);
-  const int64_t slot = slots ? slots[row] : row;
-  const int32_t s = pool[slot];
-  const float* lrow = (s >= 0 && s < S) ? la + static_cast<int64_t>(s) * V : nullptr;
-  Bits* out = reinterpret_cast<Bits*>(logits + row * row_stride);
-  const Bits ninf = Dt<T>::from_float_dev(-INFINITY);
-  for (int32_t e = c0 + threadIdx.x; e < c1; e += kThreads) {
-    const float bias = lrow ? __ldcs(lrow + e) : -INFINITY;
-    if (bias == -INFINITY) {
-      out[e] = ninf;
-    } else if (alpha != 0.0f) {
-      out[e] = Dt<T>::from_float_dev(fmaf(alpha, bias, Dt<T>::to_float(out[e])));
-    }
+// Soft rows: the state picks its allow row (which tiles and vectors are
+// live) and its lookahead row (the biases); no state = everything -inf.
+struct SoftRows {
+  static constexpr bool kSoft = true;
+  const int32_t* pool;
+  const int64_t* slots;
+  const uint32_t* bits;
+  int32_t wstride;
+  const float* la;
+  int32_t S;
+  int32_t V;
+  float alpha;
+  __device__ __forceinline__ RowInfo operator()(int32_t row) const {
+    RowInfo r;
+    r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);
+    r.lrow = r.brow ? la + static_cast<int64_t>(r.state) * V : nullptr;
+    return r;
   }
-}
+};
 
 template <typename T>
 bpd_status launch_soft_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
-                             const int32_t* pool, const int64_t* slots, const float* la, int32_t S,
-                             float alpha, cudaStream_t st) {
-  const int32_t chunk = kThreads * 32;
-  const int32_t chunks = (V + chunk - 1) / chunk;
-  const int64_t grid = static_cast<int64_t>(batch) * chunks;
-  BPD_REQUIRE(grid < 0x7FFFFFFF, "bpd_soft_apply: batch too large");
-  soft_apply_kernel<T><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
-      static_cast<T*>(logits), row_stride, V, pool, slots, la, S, alpha, chunk, chunks);
-  return check_launch("soft_apply_kernel");
+                             const SoftRows& rows, cudaStream_t st) {
+  return launch_stream_apply<T, SoftRows>(logits, row_stride, batch, V, rows, -INFINITY, st,
+                                          "bpd_soft_apply");
+}
+
+template <typename T>
+bpd_status launch_soft_step(void* logits, int64_t row_stride, int32_t batch, int32_t V,
+                            const SoftRows& rows, const DenseCommit& commit, int32_t k,
+                            cudaStream_t st) {
+  return launch_stream_step<T, SoftRows, DenseCommit>(logits, row_stride, batch, V, rows, commit,
+                                                      -INFINITY, k, st, "bpd_soft_step_greedy");
 }
 
 }  // namespace
@@ -185,23 +181,59 @@ extern "C" bpd_status bpd_soft_build_lookahead(const int32_t* tok_next, int32_t 
 extern "C" bpd_status bpd_soft_apply(void* logits, int32_t dtype, int64_t row_stride,
                                      int32_t batch, int32_t vocab_size, const int32_t* state_pool,
                                      const int64_t* slots, const float* lookahead,
+                                     const uint32_t* allow_bits, int32_t words_stride,
                                      int32_t num_states, float alpha, void* stream) {
   BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_soft_apply: bad sizes");
   if (batch == 0) return BPD_OK;
-  BPD_REQUIRE(logits && state_pool && lookahead, "bpd_soft_apply: null pointer");
+  BPD_REQUIRE(logits && state_pool && lookahead && allow_bits, "bpd_soft_apply: null pointer");
   BPD_REQUIRE(row_stride >= vocab_size, "bpd_soft_apply: row_stride < vocab");
+  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32, "bpd_soft_apply: words_stride too small");
   cudaStream_t st = as_stream(stream);
+  const SoftRows rows{const_cast<int32_t*>(state_pool), slots, allow_bits, words_stride,
+                      lookahead, num_states, vocab_size, alpha};
   switch (dtype) {
     case BPD_F32:
-      return launch_soft_apply<float>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                      lookahead, num_states, alpha, st);
+      return launch_soft_apply<float>(logits, row_stride, batch, vocab_size, rows, st);
     case BPD_BF16:
-      return launch_soft_apply<__nv_bfloat16>(logits, row_stride, batch, vocab_size, state_pool,
-                                              slots, lookahead, num_states, alpha, st);
+      return launch_soft_apply<__nv_bfloat16>(logits, row_stride, batch, vocab_size, rows, st);
     case BPD_F16:
-      return launch_soft_apply<__half>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                       lookahead, num_states, alpha, st);
+      return launch_soft_apply<__half>(logits, row_stride, batch, vocab_size, rows, st);
     default:
       return fail(BPD_ERR_INVALID, "bpd_soft_apply: unsupported logits dtype %d", dtype);
+  }
+}
+
+extern "C" bpd_status bpd_soft_step_greedy(void* logits, int32_t dtype, int64_t row_stride,
+                                           int32_t batch, int32_t vocab_size, int32_t* state_pool,
+                                           const int64_t* slots, const float* lookahead,
+                                           const uint32_t* allow_bits, int32_t words_stride,
+                                           const int32_t* tok_next, int32_t num_states,
+                                           float alpha, int64_t* token_out, int32_t* next_out,
+                                           int32_t ctas_per_row, void* stream) {
+  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_soft_step_greedy: bad sizes");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(logits && state_pool && lookahead && allow_bits && tok_next && token_out,
+              "bpd_soft_step_greedy: null pointer");
+  BPD_REQUIRE(row_stride >= vocab_size, "bpd_soft_step_greedy: row_stride < vocab");
+  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
+              "bpd_soft_step_greedy: words_stride too small");
+  BPD_REQUIRE(ctas_per_row == 0 || ctas_per_row == 1 || ctas_per_row == 2 || ctas_per_row == 4 ||
+                  ctas_per_row == 8,
+              "bpd_soft_step_greedy: ctas_per_row must be 0, 1, 2, 4 or 8");
+  const int32_t k = ctas_per_row ? ctas_per_row : auto_ctas_per_row(batch);
+  cudaStream_t st = as_stream(stream);
+  const SoftRows rows{state_pool, slots, allow_bits, words_stride, lookahead, num_states,
+                      vocab_size, alpha};
+  const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
+  switch (dtype) {
+    case BPD_F32:
+      return launch_soft_step<float>(logits, row_stride, batch, vocab_size, rows, commit, k, st);
+    case BPD_BF16:
+      return launch_soft_step<__nv_bfloat16>(logits, row_stride, batch, vocab_size, rows, commit,
+                                             k, st);
+    case BPD_F16:
+      return launch_soft_step<__half>(logits, row_stride, batch, vocab_size, rows, commit, k, st);
+    default:
+      return fail(BPD_ERR_INVALID, "bpd_soft_step_greedy: unsupported logits dtype %d", dtype);
   }
 }

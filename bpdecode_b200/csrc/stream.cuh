@@ -18,7 +18,10 @@ namespace bpd {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kVPT = 4;  // 16-byte vectors per lane per warp tile
+#ifndef BPD_VPT
+#define BPD_VPT 4
+#endif
+constexpr int kVPT = BPD_VPT;  // 16-byte vectors per lane per warp tile
 constexpr unsigned kAll = 0xFFFFFFFFu;
 
 template <typename T>
@@ -26,53 +29,111 @@ constexpr int tile_elems() {
   return 32 * kVPT * Dt<T>::kPerVec;
 }
 
-// Running first-maximal element of a thread's share of a masked row.
+// First-maximal element of a thread's share of a row, as (key, index) with
+// key = order_key(value); merged lexicographically, so the order of merging
+// does not matter.
 struct ArgState {
-  uint32_t key = 0;      // order_key of the best value seen (0 = none yet)
-  int32_t idx = INT_MAX; // its index (the first one with that key)
+  uint32_t key = 0;       // order_key of the best value seen (0 = none yet)
+  int32_t idx = INT_MAX;  // its index (the first one with that key)
 };
 
-// Key of the largest element of a 16-byte vector (NaN is the largest).
+// max() that returns NaN when either input is NaN.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Largest element of a 16-byte vector as fp32 (NaN if any element is NaN).
 template <typename T>
-__device__ __forceinline__ uint32_t vec_max_key(const uint4& v) {
+__device__ __forceinline__ float vec_max(const uint4& v) {
   if constexpr (sizeof(typename Dt<T>::Bits) == 4) {
-    const uint32_t a = max(order_key(__uint_as_float(v.x)), order_key(__uint_as_float(v.y)));
-    const uint32_t b = max(order_key(__uint_as_float(v.z)), order_key(__uint_as_float(v.w)));
-    return max(a, b);
+    return fmax_nan(fmax_nan(__uint_as_float(v.x), __uint_as_float(v.y)),
+                    fmax_nan(__uint_as_float(v.z), __uint_as_float(v.w)));
   } else if constexpr (std::is_same_v<T, __nv_bfloat16>) {
     const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&v);
     const __nv_bfloat162 m = __hmax2_nan(__hmax2_nan(p[0], p[1]), __hmax2_nan(p[2], p[3]));
-    return max(order_key(__low2float(m)), order_key(__high2float(m)));
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(&m);
+    return fmax_nan(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
   } else {
     const __half2* p = reinterpret_cast<const __half2*>(&v);
     const __half2 m = __hmax2_nan(__hmax2_nan(p[0], p[1]), __hmax2_nan(p[2], p[3]));
-    return max(order_key(__low2float(m)), order_key(__high2float(m)));
+    return fmax_nan(__low2float(m), __high2float(m));
   }
 }
 
-// Fold the vector starting at element e0 into the running best: only a vector
-// whose maximum is at least the best so far is searched for its first
-// maximal lane. Ties go to the lower index, whatever order elements are seen.
-template <typename T>
-__device__ __forceinline__ void arg_vec(ArgState& st, const uint4& v, int32_t e0) {
-  const uint32_t k = vec_max_key<T>(v);
-  if (k >= st.key) {
-    int32_t first = 0;
-#pragma unroll
-    for (int i = Dt<T>::kPerVec - 1; i >= 0; --i)
-      if (order_key(Dt<T>::to_float(vec_get<T>(v, i))) == k) first = i;
-    if (k > st.key || e0 + first < st.idx) {
-      st.key = k;
-      st.idx = e0 + first;
-    }
-  }
-}
-
-__device__ __forceinline__ void arg_one(ArgState& st, uint32_t k, int32_t idx) {
+// Fold element `idx` with value `x` into the running best (ties: lower index).
+__device__ __forceinline__ void arg_elem(ArgState& st, float x, int32_t idx) {
+  const uint32_t k = order_key(x);
   if (k > st.key || (k == st.key && idx < st.idx)) {
     st.key = k;
     st.idx = idx;
   }
+}
+
+// Running best VECTOR of a thread that visits its vectors in increasing index
+// order: the largest vector maximum (NaN above everything, -0 == +0) and the
+// first vector that reached it. Folding a vector is a few branch-free
+// instructions, the same for every lane of a warp; the element inside the
+// winning vector is found once, at the end (vec_arg_resolve).
+struct VecArg {
+  float best = 0.0f;
+  int32_t vec = INT_MAX;  // element index of the winning vector (INT_MAX: none)
+};
+
+__device__ __forceinline__ void vec_arg_fold(VecArg& a, float m, int32_t e0) {
+  const bool take = (a.vec == INT_MAX) | (m > a.best) | ((m != m) & (a.best == a.best));
+  a.best = take ? m : a.best;
+  a.vec = take ? e0 : a.vec;
+}
+
+// Merge the winning vector's first maximal element into `st`. The vector is
+// read back from `row`: this thread wrote it (or left it untouched) itself.
+template <typename T>
+__device__ __forceinline__ void vec_arg_resolve(ArgState& st, const VecArg& a, const T* row) {
+  if (a.vec == INT_MAX) return;
+  const uint4 v = *reinterpret_cast<const uint4*>(row + a.vec);
+  const uint32_t k = order_key(a.best);
+  int32_t first = 0;
+#pragma unroll
+  for (int i = Dt<T>::kPerVec - 1; i >= 0; --i)
+    if (order_key(Dt<T>::to_float(vec_get<T>(v, i))) == k) first = i;
+  if (k > st.key || (k == st.key && a.vec + first < st.idx)) {
+    st.key = k;
+    st.idx = a.vec + first;
+  }
+}
+
+// One element of apply_soft_: -inf where the bias is -inf (disallowed),
+// otherwise logits + alpha * bias (the add skipped when alpha == 0) computed
+// in fp32 and rounded once to the logits dtype.
+template <typename T>
+__device__ __forceinline__ typename Dt<T>::Bits soft_one(typename Dt<T>::Bits x, float bias,
+                                                         float alpha) {
+  if (bias == -INFINITY) return Dt<T>::from_float_dev(-INFINITY);
+  if (alpha == 0.0f) return x;
+  return Dt<T>::from_float_dev(fmaf(alpha, bias, Dt<T>::to_float(x)));
+}
+
+// soft_one over a 16-byte logits vector and its EPV biases.
+template <typename T>
+__device__ __forceinline__ uint4 soft_vec(const uint4& x, const float4* b, float alpha) {
+  using Bits = typename Dt<T>::Bits;
+  constexpr int EPV = Dt<T>::kPerVec;
+  uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int i = 0; i < EPV; ++i) {
+    const float4& f = b[i >> 2];
+    const float bi = (i & 3) == 0 ? f.x : (i & 3) == 1 ? f.y : (i & 3) == 2 ? f.z : f.w;
+    const Bits y = soft_one<T>(vec_get<T>(x, i), bi, alpha);
+    if constexpr (sizeof(Bits) == 4) {
+      w[i] = y;
+    } else {
+      w[i >> 1] = (i & 1) ? ((w[i >> 1] & 0xFFFFu) | (uint32_t(y) << 16))
+                          : ((w[i >> 1] & 0xFFFF0000u) | uint32_t(y));
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // Shared memory of one streaming CTA: a buffer of fill values that bulk
@@ -115,16 +176,24 @@ __device__ __forceinline__ void bulk_fill(void* dst, uint32_t bytes, const uint4
 //    values -- no per-element instructions -- and only waits for the engine
 //    to have read the buffer before the CTA may exit.
 // 3. The other tiles stream through registers, interleaved across warps so a
-//    CTA's accesses stay within one window: all-allowed vectors are skipped
-//    (loaded only for the argmax), rejected vectors stored, mixed ones loaded,
-//    blended and stored.
-// Elements are visited in increasing order per thread, so a strict `>` keeps
-// the first occurrence. All threads of the CTA must call this.
-template <typename T, bool kVec, bool kArgmax>
+//    CTA's accesses stay within one window: all-allowed vectors are not
+//    written (loaded only for the argmax), rejected vectors are stored without
+//    a load, mixed ones loaded, blended and stored.
+// With kArgmax a thread folds its vectors (in increasing index order) into a
+// VecArg, resolved at the end; the bulk-filled runs and the scalar tail's
+// fills only lower `fill_first`. All threads of the CTA must call this.
+//
+// With kSoft the chunk gets apply_soft_ instead of the plain mask: `lrow` is
+// the row's lookahead biases (finite only where `brow` allows, so dead tiles
+// and all-rejected vectors are the same -inf fill), and every live vector
+// loads its logits and its biases together and is always written.
+template <typename T, bool kVec, bool kArgmax, bool kSoft = false>
 __device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int32_t c1,
                                            const uint32_t* __restrict__ brow,
                                            typename Dt<T>::Bits fill, ArgState& st,
-                                           uint8_t* __restrict__ smem) {
+                                           uint8_t* __restrict__ smem,
+                                           const float* __restrict__ lrow = nullptr,
+                                           float alpha = 0.0f) {
   using Bits = typename Dt<T>::Bits;
   constexpr int EPV = Dt<T>::kPerVec;
   constexpr int TILE = tile_elems<T>();
@@ -134,7 +203,8 @@ __device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int3
   uint8_t* sdead = smem + kFillBytes;
   const int32_t lane = threadIdx.x & 31;
   const int32_t warp = threadIdx.x >> 5;
-  const uint32_t fill_key = kArgmax ? order_key(Dt<T>::to_float(fill)) : 0u;
+  int32_t fill_first = INT_MAX;  // lowest index this thread wrote `fill` to
+  VecArg va;
   const uint4 fv = vec_splat<T>(fill);
   const int32_t ntiles = (kVec && c1 > c0) ? (c1 - c0) / TILE : 0;
   uint32_t* sbits = reinterpret_cast<uint32_t*>(
@@ -169,7 +239,7 @@ __device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int3
         int32_t te = ti + 1;
         while (te < ntiles && sdead[te]) ++te;
         bulk_fill(row + c0 + ti * TILE, static_cast<uint32_t>((te - ti) * TILE * sizeof(T)), sfill);
-        if constexpr (kArgmax) arg_one(st, fill_key, c0 + ti * TILE);
+        fill_first = min(fill_first, c0 + ti * TILE);
         issued = true;
         ti = te;
       }
@@ -190,24 +260,44 @@ __device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int3
         bits[j] = (word >> ((v * EPV) & 31)) & FULL;
       }
       uint4* base = reinterpret_cast<uint4*>(row + tb);
-      uint4 val[kVPT];
+      // Lanes of a warp see different bit patterns: every step below is the
+      // same instruction stream for all of them (predicated loads and store,
+      // branch-free blend), so a warp never runs the cases one after another.
+      // Soft vectors go in groups (logits + biases in flight together).
+      constexpr int G = kSoft ? (sizeof(Bits) == 4 ? 2 : 1) : kVPT;
+      constexpr int NB = kSoft ? G * (EPV / 4) : 1;
 #pragma unroll
-      for (int j = 0; j < kVPT; ++j) {
-        const bool need = kArgmax ? (bits[j] != 0u) : (bits[j] != 0u && bits[j] != FULL);
-        if (need) val[j] = __ldcs(base + lane + 32 * j);
-      }
+      for (int g = 0; g < kVPT; g += G) {
+        uint4 val[G];
+        float4 bias[NB];
 #pragma unroll
-      for (int j = 0; j < kVPT; ++j) {
-        const int32_t e0 = tb + (lane + 32 * j) * EPV;
-        if (bits[j] == FULL) {
-          if constexpr (kArgmax) arg_vec<T>(st, val[j], e0);
-        } else if (bits[j] == 0u) {
-          __stcs(base + lane + 32 * j, fv);
-          if constexpr (kArgmax) arg_one(st, fill_key, e0);
-        } else {
-          const uint4 out = vec_blend<T>(val[j], bits[j], fill);
-          __stcs(base + lane + 32 * j, out);
-          if constexpr (kArgmax) arg_vec<T>(st, out, e0);
+        for (int jj = 0; jj < G; ++jj) {
+          const int j = g + jj;
+          const bool need = (kArgmax || kSoft) ? (bits[j] != 0u)
+                                               : (bits[j] != 0u && bits[j] != FULL);
+          val[jj] = make_uint4(0u, 0u, 0u, 0u);  // not read by the blend unless loaded
+          if (need) val[jj] = __ldcs(base + lane + 32 * j);
+          if constexpr (kSoft) {
+            const float4* lb =
+                reinterpret_cast<const float4*>(lrow + tb + (lane + 32 * j) * EPV);
+#pragma unroll
+            for (int q = 0; q < EPV / 4; ++q) {
+              bias[jj * (EPV / 4) + q] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+              if (need) bias[jj * (EPV / 4) + q] = __ldg(lb + q);
+            }
+          }
+        }
+#pragma unroll
+        for (int jj = 0; jj < G; ++jj) {
+          const int j = g + jj;
+          uint4 out;
+          if constexpr (kSoft) {
+            out = soft_vec<T>(val[jj], &bias[jj * (EPV / 4)], alpha);
+          } else {
+            out = vec_blend<T>(val[jj], bits[j], fill);
+          }
+          if (kSoft || bits[j] != FULL) __stcs(base + lane + 32 * j, out);
+          if constexpr (kArgmax) vec_arg_fold(va, vec_max<T>(out), tb + (lane + 32 * j) * EPV);
         }
       }
     }
@@ -215,12 +305,20 @@ __device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int3
   Bits* rb = reinterpret_cast<Bits*>(row);
   for (int32_t e = vend + static_cast<int32_t>(threadIdx.x); e < c1; e += kThreads) {
     const bool allowed = brow != nullptr && ((sbits[(e >> 5) - w0] >> (e & 31)) & 1u);
-    if (allowed) {
-      if constexpr (kArgmax) arg_one(st, order_key(Dt<T>::to_float(rb[e])), e);
+    if constexpr (kSoft) {
+      const Bits y = soft_one<T>(rb[e], allowed ? __ldg(lrow + e) : -INFINITY, alpha);
+      rb[e] = y;
+      if constexpr (kArgmax) arg_elem(st, Dt<T>::to_float(y), e);
+    } else if (allowed) {
+      if constexpr (kArgmax) arg_elem(st, Dt<T>::to_float(rb[e]), e);
     } else {
       rb[e] = fill;
-      if constexpr (kArgmax) arg_one(st, fill_key, e);
+      fill_first = min(fill_first, e);
     }
+  }
+  if constexpr (kArgmax) {
+    vec_arg_resolve<T>(st, va, row);
+    if (fill_first != INT_MAX) arg_elem(st, Dt<T>::to_float(fill), fill_first);
   }
 }
 
@@ -233,6 +331,65 @@ struct RowInfo {
   const uint32_t* brow;
   int32_t state;
   int64_t slot;
+  const float* lrow = nullptr;  // soft rows: the lookahead biases of the state
+};
+
+// Rows functors say whether they carry lookahead biases (Rows::kSoft) and
+// then hold the bias scale `alpha`.
+template <class Rows>
+__device__ __forceinline__ float rows_alpha(const Rows& r) {
+  if constexpr (Rows::kSoft) {
+    return r.alpha;
+  } else {
+    return 0.0f;
+  }
+}
+
+// Dense rows: a row's state from the pool (through its slot) picks an allow
+// row; DenseCommit writes the chosen token's next state (ops.py:301-306).
+__device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__ pool,
+                                                     const int64_t* __restrict__ slots,
+                                                     int32_t row, const uint32_t* __restrict__ bits,
+                                                     int32_t wstride, int32_t S, int32_t* state,
+                                                     int64_t* slot_out) {
+  const int64_t slot = slots ? slots[row] : row;
+  const int32_t s = pool[slot];
+  *state = s;
+  if (slot_out) *slot_out = slot;
+  return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
+}
+
+struct DenseRows {
+  static constexpr bool kSoft = false;
+  const int32_t* pool;
+  const int64_t* slots;
+  const uint32_t* bits;
+  int32_t wstride;
+  int32_t S;
+  __device__ __forceinline__ RowInfo operator()(int32_t row) const {
+    RowInfo r;
+    r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);
+    return r;
+  }
+};
+
+// Dense commit of the chosen token: next = tok_next[state, token] (ops.py:301-306).
+struct DenseCommit {
+  int32_t* pool;
+  const int32_t* tok_next;
+  int32_t S;
+  int32_t V;
+  int64_t* token_out;
+  int32_t* next_out;
+  __device__ __forceinline__ void operator()(int32_t row, const RowInfo& r, int32_t tok) const {
+    const int32_t s = r.state;
+    const int32_t next = (s >= 0 && s < S && tok >= 0 && tok < V)
+                             ? tok_next[static_cast<int64_t>(s) * V + tok]
+                             : -1;
+    pool[r.slot] = next;
+    token_out[row] = tok;
+    if (next_out) next_out[row] = next;
+  }
 };
 
 // Register cap (resident CTAs per SM) and warp tiles per warp of one apply
@@ -259,31 +416,23 @@ __global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
   const RowInfo info = rows(row);
   extern __shared__ __align__(16) uint8_t smem[];
   ArgState st;
-  mask_chunk<T, kVec, false>(logits + row * row_stride, c0, c1, info.brow, fill, st, smem);
+  mask_chunk<T, kVec, false, Rows::kSoft>(logits + row * row_stride, c0, c1, info.brow, fill, st,
+                                          smem, info.lrow, rows_alpha(rows));
 }
 
-// Fused greedy step: a thread-block cluster of `k` CTAs owns one row; every
-// CTA masks its slice and reduces its first-maximal element; the partials are
-// written into rank 0's shared memory (distributed shared memory), and after
-// one cluster barrier rank 0 hands the winning token to `commit`.
-template <typename T, bool kVec, class Rows, class Commit>
-__global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
-    stream_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
-                       Commit commit, typename Dt<T>::Bits fill, int32_t chunk) {
+// End of a fused step: reduce every thread's first-maximal element to the
+// CTA's, write it into rank 0's shared memory (distributed shared memory),
+// and after one cluster barrier let rank 0 commit the row's winning token.
+// All threads of every CTA of the cluster must call this.
+template <class Commit>
+__device__ __forceinline__ void cluster_commit(const ArgState& st, int32_t row,
+                                               const RowInfo& info, const Commit& commit) {
   __shared__ uint64_t warp_best[kWarps];
   __shared__ uint64_t cluster_best[8];
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int32_t k = static_cast<int32_t>(cluster.num_blocks());
   const int32_t rank = static_cast<int32_t>(cluster.block_rank());
-  const int32_t row = blockIdx.x / k;
-  const int32_t c0 = rank * chunk;
-  const int32_t c1 = min(V, c0 + chunk);
-  const RowInfo info = rows(row);
-  extern __shared__ __align__(16) uint8_t smem[];
-  ArgState st;
-  mask_chunk<T, kVec, true>(logits + row * row_stride, c0, c1, info.brow, fill, st, smem);
-
   const uint64_t mine = warp_max_u64(pack_arg(st.key, st.idx));
   const int32_t lane = threadIdx.x & 31;
   const int32_t warp = threadIdx.x >> 5;
@@ -305,8 +454,37 @@ __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
   }
 }
 
+// Fused greedy step: a thread-block cluster of `k` CTAs owns one row; every
+// CTA masks its slice and reduces its first-maximal element; the partials are
+// written into rank 0's shared memory (distributed shared memory), and after
+// one cluster barrier rank 0 hands the winning token to `commit`.
+template <typename T, bool kVec, class Rows, class Commit>
+__global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
+    stream_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
+                       Commit commit, typename Dt<T>::Bits fill, int32_t chunk) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int32_t k = static_cast<int32_t>(cluster.num_blocks());
+  const int32_t rank = static_cast<int32_t>(cluster.block_rank());
+  const int32_t row = blockIdx.x / k;
+  const int32_t c0 = rank * chunk;
+  const int32_t c1 = min(V, c0 + chunk);
+  const RowInfo info = rows(row);
+  extern __shared__ __align__(16) uint8_t smem[];
+  ArgState st;
+  mask_chunk<T, kVec, true, Rows::kSoft>(logits + row * row_stride, c0, c1, info.brow, fill, st,
+                                         smem, info.lrow, rows_alpha(rows));
+  cluster_commit(st, row, info, commit);
+}
+
 inline bool rows_aligned(const void* logits, int64_t row_stride, size_t esize) {
   return aligned16(logits) && (row_stride * static_cast<int64_t>(esize)) % 16 == 0;
+}
+
+// The vector path also needs 16-byte aligned lookahead rows (V % 4 == 0).
+template <class Rows>
+bool vec_ok(const void* logits, int64_t row_stride, size_t esize, int32_t V) {
+  return rows_aligned(logits, row_stride, esize) && (!Rows::kSoft || V % 4 == 0);
 }
 
 template <typename T, class Rows>
@@ -321,7 +499,7 @@ bpd_status launch_stream_apply(void* logits, int64_t row_stride, int32_t batch, 
   const auto fill = Dt<T>::from_float_host(neg_inf);
   const size_t smem = stream_smem_bytes<T>(chunk);
   T* lg = static_cast<T*>(logits);
-  if (rows_aligned(logits, row_stride, sizeof(T))) {
+  if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
     stream_apply_kernel<T, true, Rows><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
         lg, row_stride, V, rows, fill, chunk, chunks);
   } else {
@@ -366,7 +544,7 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   cfg.numAttrs = 1;
   T* lg = static_cast<T*>(logits);
   cudaError_t e;
-  if (rows_aligned(logits, row_stride, sizeof(T))) {
+  if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
     e = cudaLaunchKernelEx(&cfg, stream_step_kernel<T, true, Rows, Commit>, lg, row_stride, V,
                            rows, commit, fill, chunk);
   } else {

@@ -459,10 +459,11 @@ def apply_soft_(
     code = _check_logits(logits, fsa.vocab_size)
     st = _as_i32(states, B, fsa.device)
     la = fsa.lookahead.contiguous()
+    bits = fsa.dense_tables()[1]
     L = _capi.lib()
     L.check(L.bpd_soft_apply(logits.data_ptr(), code, logits.stride(0), B, fsa.vocab_size,
-                             st.data_ptr(), None, la.data_ptr(), fsa.num_states, float(alpha),
-                             _stream(logits)))
+                             st.data_ptr(), None, la.data_ptr(), bits.data_ptr(), bits.shape[1],
+                             fsa.num_states, float(alpha), _stream(logits)))
     return logits
 
 
@@ -497,8 +498,42 @@ def step_greedy_(
     return tokens, nxt
 
 
+def soft_step_greedy_(
+    logits: torch.Tensor,
+    fsa: FsaTensors,
+    state_pool: torch.Tensor,
+    slots: torch.Tensor | None = None,
+    alpha: float = 1.0,
+    ctas_per_row: int = 0,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """NEW, fused: ``apply_soft_`` in place, the first maximal token of every
+    biased row, and its commit into ``state_pool[slots[b]]``. Returns
+    (tokens int64 [B], next states int32 [B]); identical to ``apply_soft_`` +
+    ``logits.argmax(-1)`` + ``advance_state``, in one launch."""
+    if fsa.lookahead is None or fsa.tok_next is None:
+        raise ValueError("fsa has no lookahead table; build with dense + with_lookahead")
+    B = int(logits.shape[0])
+    code = _check_logits(logits, fsa.vocab_size)
+    _require_cuda(state_pool, "state_pool")
+    if state_pool.dtype != torch.int32 or not state_pool.is_contiguous():
+        raise RuntimeError("bpdecode_b200: state_pool must be a contiguous int32 tensor")
+    if slots is not None and (slots.dtype != torch.int64 or slots.numel() != B):
+        raise RuntimeError("bpdecode_b200: slots must be int64 [batch]")
+    la = fsa.lookahead.contiguous()
+    tok_next, bits = fsa.dense_tables()
+    tokens = torch.empty(B, dtype=torch.int64, device=logits.device)
+    nxt = torch.empty(B, dtype=torch.int32, device=logits.device)
+    L = _capi.lib()
+    L.check(L.bpd_soft_step_greedy(
+        logits.data_ptr(), code, logits.stride(0), B, fsa.vocab_size, state_pool.data_ptr(),
+        _ptr(slots), la.data_ptr(), bits.data_ptr(), bits.shape[1], tok_next.data_ptr(),
+        fsa.num_states, float(alpha), tokens.data_ptr(), nxt.data_ptr(), int(ctas_per_row),
+        _stream(logits)))
+    return tokens, nxt
+
+
 __all__ = [
     "DENSE_AUTO_LIMIT", "FsaTensors", "Vocabulary", "advance_state", "apply_mask_",
     "apply_soft_", "build_allow_bits", "build_lookahead", "build_token_transitions",
-    "compute_mask", "dfa_arrays", "step_greedy_", "words_stride",
+    "compute_mask", "dfa_arrays", "soft_step_greedy_", "step_greedy_", "words_stride",
 ]

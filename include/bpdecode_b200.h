@@ -173,11 +173,29 @@ bpd_status bpd_soft_build_lookahead(
 
 /* In place: logits += alpha * bias on entries where bias is finite (skipped
  * when alpha == 0), then logits = -inf where bias is -inf; bias =
- * lookahead[state], all -inf for state < 0. Replaces ops.py:239-259. */
+ * lookahead[state], all -inf for state < 0. Replaces ops.py:239-259.
+ * allow_bits / words_stride: the packed allow rows of the same states
+ * (bpd_dense_build_allow_bits). A bias is finite only where its token is
+ * allowed (true of every table bpd_soft_build_lookahead makes from the same
+ * tok_next), so tiles without an allowed token are written without reading
+ * the logits or the biases. */
 bpd_status bpd_soft_apply(
     void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
     int32_t vocab_size, const int32_t* state_pool, const int64_t* slots,
-    const float* lookahead, int32_t num_states, float alpha, void* stream);
+    const float* lookahead, const uint32_t* allow_bits, int32_t words_stride,
+    int32_t num_states, float alpha, void* stream);
+
+/* NEW fused soft step: bpd_soft_apply (with alpha), then the first maximal
+ * token of every row (torch.argmax order) into token_out (int64 [batch]) and
+ * its commit next = tok_next[state, token] into state_pool[slots[b]] (and
+ * next_out, may be NULL). Same results as apply_soft_ + argmax + commit
+ * (batch.py:192-215) with one pass over the logits fewer. */
+bpd_status bpd_soft_step_greedy(
+    void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
+    int32_t vocab_size, int32_t* state_pool, const int64_t* slots,
+    const float* lookahead, const uint32_t* allow_bits, int32_t words_stride,
+    const int32_t* tok_next, int32_t num_states, float alpha,
+    int64_t* token_out, int32_t* next_out, int32_t ctas_per_row, void* stream);
 
 /* --------------------------------------------------------------------------
  * Pushdown automaton (context-free grammars)

@@ -386,6 +386,36 @@ def test_mixed_grammar_batch_equals_separate_batches() -> None:
                 assert mixed.is_complete((g, r)) == singles[g].is_complete((g, r))
 
 
+def test_reset_many_equals_per_row_reset() -> None:
+    """reset_many(ids) puts exactly the named rows back at their own
+    grammar's start state, like reset() per id, and leaves the rest alone."""
+    from bpdecode_b200.batch import ConstraintBatch
+    from bpdecode_b200.ops import FsaTensors
+
+    patterns = list(SMALL["meta/patterns"])
+    v = vocab_of("dense")
+    fsas = [FsaTensors.from_arrays(small_dfa(SMALL, "dense", i), v).to("cuda")
+            for i in range(len(patterns))]
+    a = ConstraintBatch(fsas, capacity=3 * len(fsas))
+    b = ConstraintBatch(fsas, capacity=3 * len(fsas))
+    ids = [(g, r) for g in range(len(fsas)) for r in range(3)]
+    for i in ids:
+        a.add(i, grammar=i[0])
+        b.add(i, grammar=i[0])
+    gen = torch.Generator().manual_seed(9)
+    for step in range(8):
+        logits = torch.randn(len(ids), v.size, generator=gen).cuda()
+        ta = a.step_greedy(ids, logits.clone())
+        tb = b.step_greedy(ids, logits.clone())
+        assert torch.equal(ta, tb)
+        if step % 3 == 2:
+            some = [i for i in ids if (i[1] + step) % 2]
+            a.reset_many(some)
+            for i in some:
+                b.reset(i)
+            assert [a.state_of(i) for i in ids] == [b.state_of(i) for i in ids]
+
+
 def test_empty_batch_and_cpu_tensors_fail_loudly() -> None:
     from bpdecode_b200 import ops
 
