@@ -48,8 +48,9 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "bpd_dense_apply_mask": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _I32, _I32, _F, _P]),
     "bpd_dense_advance": (_I32, [_P, _P, _I32, _P, _I32, _P, _I32, _I32, _P, _I32, _P]),
     "bpd_dense_mask_bits": (_I32, [_P, _P, _I32, _P, _I32, _I32, _I32, _P, _P]),
+    "bpd_step_scratch_bytes": (C.c_size_t, [_I32]),
     "bpd_dense_step_greedy": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _F,
-                                     _P, _P, _I32, _P]),
+                                     _P, _P, _I32, _P, _P]),
     "bpd_walk_apply_mask": (_I32, [_P, _I32, _I64, _I32, _P, _I32, _I32, _P, _P, _I32, _P, _P,
                                    _I32, _I32, _P, _F, _P]),
     "bpd_walk_mask_bits": (_I32, [_P, _I32, _I32, _P, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _P,
@@ -60,7 +61,7 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "bpd_soft_build_lookahead": (_I32, [_P, _I32, _I32, _P, _P, _I32, _I32, _P, _P, _P]),
     "bpd_soft_apply": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _P, _I32, _I32, _F, _P]),
     "bpd_soft_step_greedy": (_I32, [_P, _I32, _I64, _I32, _I32, _P, _P, _P, _P, _I32, _P, _I32,
-                                    _F, _P, _P, _I32, _P]),
+                                    _F, _P, _P, _I32, _P, _P]),
     "bpd_pda_init": (_I32, [C.POINTER(PdaGrammar), _P, _P]),
     "bpd_pda_memo_bytes": (_S, [_I32, _I32]),
     "bpd_pda_memo_reset": (_I32, [_P, _I32, _I32, _P]),

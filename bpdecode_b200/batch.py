@@ -170,6 +170,9 @@ class ConstraintBatch:
         self._t = _Tables(grammars)
         self.capacity = capacity
         self._state = torch.full((capacity,), FREE, dtype=torch.int32, device=self.device)
+        # scratch of the fused steps (zero; the kernels leave it zero)
+        self._scratch = torch.zeros(_capi.lib().bpd_step_scratch_bytes(max(capacity, 1)),
+                                    dtype=torch.uint8, device=self.device)
         self._slot_of: dict[Hashable, int] = {}
         self._grammar_of: dict[Hashable, int] = {}
         self._free: list[int] = list(reversed(range(capacity)))
@@ -304,7 +307,7 @@ class ConstraintBatch:
         seq_ids: Sequence[Hashable],
         logits: torch.Tensor,
         neg_inf: float = float("-inf"),
-        ctas_per_row: int = 0,
+        chunks_per_row: int = 0,
     ) -> torch.Tensor:
         """NEW: ``apply_mask`` + ``logits.argmax(-1)`` + ``commit`` in one
         launch. Masks ``logits`` in place and returns the chosen tokens (int64,
@@ -321,7 +324,7 @@ class ConstraintBatch:
             logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
             slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1],
             t.tok_next.data_ptr(), t.num_states, float(neg_inf), tokens.data_ptr(), None,
-            int(ctas_per_row), _stream(logits)))
+            int(chunks_per_row), self._scratch.data_ptr(), _stream(logits)))
         return tokens
 
     def soft_step_greedy(
@@ -329,7 +332,7 @@ class ConstraintBatch:
         seq_ids: Sequence[Hashable],
         logits: torch.Tensor,
         alpha: float = 1.0,
-        ctas_per_row: int = 0,
+        chunks_per_row: int = 0,
     ) -> torch.Tensor:
         """NEW: ``apply_soft`` + ``logits.argmax(-1)`` + ``commit`` in one
         launch. Biases ``logits`` in place and returns the chosen tokens
@@ -348,7 +351,8 @@ class ConstraintBatch:
             logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
             slots.data_ptr(), t.lookahead.data_ptr(), t.allow_bits.data_ptr(),
             t.allow_bits.shape[1], t.tok_next.data_ptr(), t.num_states, float(alpha),
-            tokens.data_ptr(), None, int(ctas_per_row), _stream(logits)))
+            tokens.data_ptr(), None, int(chunks_per_row), self._scratch.data_ptr(),
+            _stream(logits)))
         return tokens
 
     # --- queries ------------------------------------------------------

@@ -87,6 +87,8 @@ struct Dt<__half> {
   __device__ static Bits from_float_dev(float f) { return __half_as_ushort(__float2half_rn(f)); }
 };
 
+constexpr size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
 __device__ __forceinline__ uint32_t vec_word(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }

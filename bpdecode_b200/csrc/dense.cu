@@ -131,10 +131,12 @@ template <typename T>
 bpd_status launch_step(void* logits, int64_t row_stride, int32_t batch, int32_t V, int32_t* pool,
                        const int64_t* slots, const uint32_t* bits, int32_t wstride,
                        const int32_t* tok_next, int32_t S, float neg_inf, int64_t* token_out,
-                       int32_t* next_out, int32_t k, cudaStream_t st) {
+                       int32_t* next_out, int32_t chunks_per_row, void* scratch,
+                       cudaStream_t st) {
   return launch_stream_step<T, DenseRows, DenseCommit>(
       logits, row_stride, batch, V, DenseRows{pool, slots, bits, wstride, S},
-      DenseCommit{pool, tok_next, S, V, token_out, next_out}, neg_inf, k, st, "dense step kernel");
+      DenseCommit{pool, tok_next, S, V, token_out, next_out}, neg_inf, chunks_per_row, scratch,
+      st, "dense step kernel");
 }
 
 }  // namespace
@@ -230,13 +232,17 @@ extern "C" bpd_status bpd_dense_mask_bits(const int32_t* state_pool, const int64
   return check_launch("dense_mask_bits_kernel");
 }
 
+extern "C" size_t bpd_step_scratch_bytes(int32_t batch) {
+  return step_scratch_bytes(batch > 0 ? batch : 0);
+}
+
 extern "C" bpd_status bpd_dense_step_greedy(void* logits, int32_t dtype, int64_t row_stride,
                                             int32_t batch, int32_t vocab_size, int32_t* state_pool,
                                             const int64_t* slots, const uint32_t* allow_bits,
                                             int32_t words_stride, const int32_t* tok_next,
                                             int32_t num_states, float neg_inf, int64_t* token_out,
-                                            int32_t* next_out, int32_t ctas_per_row,
-                                            void* stream) {
+                                            int32_t* next_out, int32_t chunks_per_row,
+                                            void* step_scratch, void* stream) {
   BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_dense_step_greedy: bad sizes");
   if (batch == 0) return BPD_OK;
   BPD_REQUIRE(logits && state_pool && allow_bits && tok_next && token_out,
@@ -245,23 +251,21 @@ extern "C" bpd_status bpd_dense_step_greedy(void* logits, int32_t dtype, int64_t
   BPD_REQUIRE(row_stride >= vocab_size, "bpd_dense_step_greedy: row_stride < vocab");
   BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
               "bpd_dense_step_greedy: words_stride too small");
-  BPD_REQUIRE(ctas_per_row == 0 || ctas_per_row == 1 || ctas_per_row == 2 || ctas_per_row == 4 ||
-                  ctas_per_row == 8,
-              "bpd_dense_step_greedy: ctas_per_row must be 0, 1, 2, 4 or 8");
-  const int32_t k = ctas_per_row ? ctas_per_row : auto_ctas_per_row(batch);
+  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
+              "bpd_dense_step_greedy: chunks_per_row must be in [0, 4096]");
   cudaStream_t st = as_stream(stream);
   switch (dtype) {
     case BPD_F32:
       return launch_step<float>(logits, row_stride, batch, vocab_size, state_pool, slots,
                                 allow_bits, words_stride, tok_next, num_states, neg_inf,
-                                token_out, next_out, k, st);
+                                token_out, next_out, chunks_per_row, step_scratch, st);
     case BPD_BF16:
       return launch_step<__nv_bfloat16>(logits, row_stride, batch, vocab_size, state_pool, slots,
                                         allow_bits, words_stride, tok_next, num_states, neg_inf,
-                                        token_out, next_out, k, st);
+                                        token_out, next_out, chunks_per_row, step_scratch, st);
     default:
       return launch_step<__half>(logits, row_stride, batch, vocab_size, state_pool, slots,
                                  allow_bits, words_stride, tok_next, num_states, neg_inf,
-                                 token_out, next_out, k, st);
+                                 token_out, next_out, chunks_per_row, step_scratch, st);
   }
 }

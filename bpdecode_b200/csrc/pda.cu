@@ -206,7 +206,6 @@ struct Memo {
   int32_t ws;       // words per allow row (multiple of 4)
 };
 
-constexpr size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
 constexpr int32_t words_stride(int32_t vocab) { return ((((vocab + 31) / 32) + 3) / 4) * 4; }
 
@@ -242,6 +241,8 @@ struct Work {
   int32_t dcap;      // power of two >= 2 * batch
   int32_t* counters; // [4] right after dedup (cleared with it): representatives,
                      //     next compute item, next first-byte item
+  void* step;        // scratch of the fused step (cleared with dedup)
+  size_t clear_bytes;  // bytes from dedup that every mask pipeline zeroes
   int32_t* reps;     // [batch] representative rows, in claim order
   int32_t* kind;     // [batch]
   int32_t* ref;      // [batch] memo entry (kHit, kRep with memo), rep row (kAlias), -1
@@ -264,6 +265,9 @@ Work work_view(void* base, int32_t batch, int32_t vocab) {
   w.dedup = reinterpret_cast<int32_t*>(p);
   w.counters = w.dedup + w.dcap;
   p += align256(sizeof(int32_t) * (w.dcap + 4));
+  w.step = p;
+  p += step_scratch_bytes(batch);
+  w.clear_bytes = static_cast<size_t>(p - static_cast<char*>(base));
   w.reps = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * batch);
   w.kind = reinterpret_cast<int32_t*>(p);
@@ -282,7 +286,8 @@ Work work_view(void* base, int32_t batch, int32_t vocab) {
 
 constexpr size_t work_bytes(int32_t batch, int32_t vocab) {
   const int32_t dcap = pow2_at_least(2 * batch > 2 ? 2 * batch : 2);
-  return align256(sizeof(int32_t) * (dcap + 4)) + 3 * align256(sizeof(int32_t) * batch) +
+  return align256(sizeof(int32_t) * (dcap + 4)) + step_scratch_bytes(batch) +
+         3 * align256(sizeof(int32_t) * batch) +
          align256(sizeof(uint64_t) * batch) + align256(sizeof(uint32_t) * 8 * batch) +
          align256(sizeof(int32_t) * batch) +
          align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(batch));
@@ -685,7 +690,7 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
               "memo capacity must be a power of two");
   Memo memo = memo_view(memo_mem, cap, g->vocab_size);
   Work w = work_view(workspace, batch, g->vocab_size);
-  cudaError_t e = cudaMemsetAsync(w.dedup, 0, sizeof(int32_t) * (w.dcap + 4), st);
+  cudaError_t e = cudaMemsetAsync(w.dedup, 0, w.clear_bytes, st);
   if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memset dedup: %s", cudaGetErrorString(e));
   lookup_kernel<<<(batch + kLookupWarps - 1) / kLookupWarps, kLookupWarps * 32, 0, st>>>(
       *g, pool, slots, broken, batch, memo, w);
@@ -713,9 +718,10 @@ bpd_status launch_pda_apply(void* logits, int64_t row_stride, int32_t batch, int
 template <typename T>
 bpd_status launch_pda_step(void* logits, int64_t row_stride, int32_t batch, int32_t V,
                            const Memo& memo, const Work& w, float neg_inf, int64_t* token_out,
-                           int32_t k, cudaStream_t st) {
+                           int32_t chunks_per_row, cudaStream_t st) {
   return launch_stream_step<T, PdaRows, TokenOut>(logits, row_stride, batch, V, PdaRows{memo, w},
-                                                  TokenOut{token_out}, neg_inf, k, st,
+                                                  TokenOut{token_out}, neg_inf, chunks_per_row,
+                                                  w.step, st,
                                                   "pda step kernel");
 }
 
@@ -808,21 +814,20 @@ extern "C" bpd_status bpd_pda_step_greedy(
     const bpd_pda_grammar* g, void* logits, int32_t dtype, int64_t row_stride,
     int32_t* config_pool, const int64_t* slots, uint8_t* broken, int32_t batch, void* memo,
     int32_t memo_capacity, void* workspace, float neg_inf, int64_t* token_out,
-    int32_t* status_out, int32_t ctas_per_row, void* stream) {
+    int32_t* status_out, int32_t chunks_per_row, void* stream) {
   BPD_REQUIRE(batch >= 0, "bpd_pda_step_greedy: bad batch");
   if (batch == 0) return BPD_OK;
   BPD_REQUIRE(logits != nullptr && token_out != nullptr, "bpd_pda_step_greedy: null pointer");
   BPD_REQUIRE(g && row_stride >= g->vocab_size, "bpd_pda_step_greedy: row_stride < vocab");
-  BPD_REQUIRE(ctas_per_row == 0 || ctas_per_row == 1 || ctas_per_row == 2 || ctas_per_row == 4 ||
-                  ctas_per_row == 8,
-              "bpd_pda_step_greedy: ctas_per_row must be 0, 1, 2, 4 or 8");
+  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
+              "bpd_pda_step_greedy: chunks_per_row must be in [0, 4096]");
   cudaStream_t st = as_stream(stream);
   Memo m;
   Work w;
   bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
                                     workspace, &m, &w, st);
   if (rc) return rc;
-  const int32_t k = ctas_per_row ? ctas_per_row : auto_ctas_per_row(batch);
+  const int32_t k = chunks_per_row;
   switch (dtype) {
     case BPD_F32:
       rc = launch_pda_step<float>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,

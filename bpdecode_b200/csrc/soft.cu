@@ -134,10 +134,11 @@ bpd_status launch_soft_apply(void* logits, int64_t row_stride, int32_t batch, in
 
 template <typename T>
 bpd_status launch_soft_step(void* logits, int64_t row_stride, int32_t batch, int32_t V,
-                            const SoftRows& rows, const DenseCommit& commit, int32_t k,
-                            cudaStream_t st) {
+                            const SoftRows& rows, const DenseCommit& commit,
+                            int32_t chunks_per_row, void* scratch, cudaStream_t st) {
   return launch_stream_step<T, SoftRows, DenseCommit>(logits, row_stride, batch, V, rows, commit,
-                                                      -INFINITY, k, st, "bpd_soft_step_greedy");
+                                                      -INFINITY, chunks_per_row, scratch, st,
+                                                      "bpd_soft_step_greedy");
 }
 
 }  // namespace
@@ -209,7 +210,8 @@ extern "C" bpd_status bpd_soft_step_greedy(void* logits, int32_t dtype, int64_t 
                                            const uint32_t* allow_bits, int32_t words_stride,
                                            const int32_t* tok_next, int32_t num_states,
                                            float alpha, int64_t* token_out, int32_t* next_out,
-                                           int32_t ctas_per_row, void* stream) {
+                                           int32_t chunks_per_row, void* step_scratch,
+                                           void* stream) {
   BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_soft_step_greedy: bad sizes");
   if (batch == 0) return BPD_OK;
   BPD_REQUIRE(logits && state_pool && lookahead && allow_bits && tok_next && token_out,
@@ -217,22 +219,22 @@ extern "C" bpd_status bpd_soft_step_greedy(void* logits, int32_t dtype, int64_t 
   BPD_REQUIRE(row_stride >= vocab_size, "bpd_soft_step_greedy: row_stride < vocab");
   BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
               "bpd_soft_step_greedy: words_stride too small");
-  BPD_REQUIRE(ctas_per_row == 0 || ctas_per_row == 1 || ctas_per_row == 2 || ctas_per_row == 4 ||
-                  ctas_per_row == 8,
-              "bpd_soft_step_greedy: ctas_per_row must be 0, 1, 2, 4 or 8");
-  const int32_t k = ctas_per_row ? ctas_per_row : auto_ctas_per_row(batch);
+  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
+              "bpd_soft_step_greedy: chunks_per_row must be in [0, 4096]");
   cudaStream_t st = as_stream(stream);
   const SoftRows rows{state_pool, slots, allow_bits, words_stride, lookahead, num_states,
                       vocab_size, alpha};
   const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
   switch (dtype) {
     case BPD_F32:
-      return launch_soft_step<float>(logits, row_stride, batch, vocab_size, rows, commit, k, st);
+      return launch_soft_step<float>(logits, row_stride, batch, vocab_size, rows, commit,
+                                     chunks_per_row, step_scratch, st);
     case BPD_BF16:
       return launch_soft_step<__nv_bfloat16>(logits, row_stride, batch, vocab_size, rows, commit,
-                                             k, st);
+                                             chunks_per_row, step_scratch, st);
     case BPD_F16:
-      return launch_soft_step<__half>(logits, row_stride, batch, vocab_size, rows, commit, k, st);
+      return launch_soft_step<__half>(logits, row_stride, batch, vocab_size, rows, commit,
+                                      chunks_per_row, step_scratch, st);
     default:
       return fail(BPD_ERR_INVALID, "bpd_soft_step_greedy: unsupported logits dtype %d", dtype);
   }

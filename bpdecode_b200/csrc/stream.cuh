@@ -10,8 +10,6 @@
 #include <climits>
 #include <type_traits>
 
-#include <cooperative_groups.h>
-
 #include "common.cuh"
 
 namespace bpd {
@@ -136,19 +134,17 @@ __device__ __forceinline__ uint4 soft_vec(const uint4& x, const float4* b, float
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Shared memory of one streaming CTA: a buffer of fill values that bulk
-// stores copy from, one flag byte per warp tile, then the staged allow words.
+// Shared memory of a streaming CTA: kFillBytes of the fill value, the source
+// of the bulk (TMA engine) stores that write fully rejected tiles.
 constexpr int32_t kFillBytes = 8192;
 
+// Fill the buffer and make it visible to the bulk-copy engine.
 template <typename T>
-__host__ __device__ constexpr int32_t stream_tiles(int32_t chunk) {
-  return (chunk + tile_elems<T>() - 1) / tile_elems<T>();
-}
-
-template <typename T>
-__host__ __device__ constexpr size_t stream_smem_bytes(int32_t chunk) {
-  return kFillBytes + ((static_cast<size_t>(stream_tiles<T>(chunk)) + 15) & ~static_cast<size_t>(15)) +
-         sizeof(uint32_t) * static_cast<size_t>((chunk + 31) / 32 + 1);
+__device__ __forceinline__ void fill_init(uint8_t* smem, typename Dt<T>::Bits fill) {
+  uint4* sfill = reinterpret_cast<uint4*>(smem);
+  const uint4 fv = vec_splat<T>(fill);
+  for (int32_t i = threadIdx.x; i < kFillBytes / 16; i += kThreads) sfill[i] = fv;
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Bulk (TMA engine) store of `bytes` (a multiple of 16) of fill values to a
@@ -164,147 +160,141 @@ __device__ __forceinline__ void bulk_fill(void* dst, uint32_t bytes, const uint4
   }
 }
 
-// Masks [c0, c1) of `row` (c0 a multiple of the warp tile, so allow words line
-// up) against allow row `brow` (nullptr = reject everything). With kArgmax the
-// thread also tracks the first maximal element of the masked row (rejected
-// elements count with the fill value, exactly as torch.argmax sees the row).
+// Warp tiles whose allow words a warp loads at once.
+constexpr int kGroupTiles = 4;
+
+// One warp masks [e0, e1) of `row` (e0 a multiple of the warp tile, so allow
+// words line up) against allow row `brow` (nullptr = reject everything); no
+// barrier, no shared state with the CTA's other warps except the read-only
+// fill buffer. With kArgmax each lane also tracks the first maximal element
+// of its share of the masked row (rejected elements count with the fill
+// value, as torch.argmax sees the row).
 //
-// 1. The chunk's allow words are staged into shared memory with independent
-//    loads (one latency for the chunk, not one dependent L2 trip per tile).
-// 2. Tiles (TILE elements) with no allowed token are flagged; thread 0 writes
-//    every run of them with the bulk-copy (TMA) engine from a buffer of fill
-//    values -- no per-element instructions -- and only waits for the engine
-//    to have read the buffer before the CTA may exit.
-// 3. The other tiles stream through registers, interleaved across warps so a
-//    CTA's accesses stay within one window: all-allowed vectors are not
-//    written (loaded only for the argmax), rejected vectors are stored without
-//    a load, mixed ones loaded, blended and stored.
-// With kArgmax a thread folds its vectors (in increasing index order) into a
-// VecArg, resolved at the end; the bulk-filled runs and the scalar tail's
-// fills only lower `fill_first`. All threads of the CTA must call this.
+// Per group of kGroupTiles tiles (TILE elements each):
+// 1. every lane loads its allow word of each tile (independent loads, one
+//    latency for the group) and one vote per tile finds the tiles with no
+//    allowed token;
+// 2. lane 0 writes each run of such tiles with the bulk-copy engine from the
+//    fill buffer -- no per-element instructions, nothing waited for until the
+//    warp exits (`issued` tells the caller to wait then);
+// 3. the other tiles stream through registers with one instruction stream
+//    for all lanes whatever their bit pattern: predicated loads and stores,
+//    branch-free blend. All-allowed vectors are not written (loaded only for
+//    the argmax), rejected ones stored without a load, mixed ones loaded,
+//    blended and stored.
+// A lane visits its vectors in increasing index order and folds them into a
+// VecArg, resolved at the end; bulk-filled runs and the scalar tail's fills
+// only lower `fill_first`.
 //
-// With kSoft the chunk gets apply_soft_ instead of the plain mask: `lrow` is
+// With kSoft the span gets apply_soft_ instead of the plain mask: `lrow` is
 // the row's lookahead biases (finite only where `brow` allows, so dead tiles
-// and all-rejected vectors are the same -inf fill), and every live vector
-// loads its logits and its biases together and is always written.
-template <typename T, bool kVec, bool kArgmax, bool kSoft = false>
-__device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int32_t c1,
-                                           const uint32_t* __restrict__ brow,
-                                           typename Dt<T>::Bits fill, ArgState& st,
-                                           uint8_t* __restrict__ smem,
-                                           const float* __restrict__ lrow = nullptr,
-                                           float alpha = 0.0f) {
+// and all-rejected vectors are the same -inf fill), and a live vector loads
+// its logits and its biases together and is always written.
+//
+// The warp's tiles start at e0 + i * tstep (i < nt; tstep = TILE: one
+// contiguous span, whose dead tiles merge into runs), then it handles the
+// scalar elements [s0, s1) one per lane.
+template <typename T, bool kVec, bool kArgmax, bool kSoft>
+__device__ __forceinline__ void warp_span(T* __restrict__ row, int32_t e0, int32_t nt,
+                                          int32_t tstep, int32_t s0, int32_t s1,
+                                          const uint32_t* __restrict__ brow,
+                                          typename Dt<T>::Bits fill, const uint4* sfill,
+                                          const float* __restrict__ lrow, float alpha,
+                                          ArgState& st, bool& issued) {
   using Bits = typename Dt<T>::Bits;
   constexpr int EPV = Dt<T>::kPerVec;
   constexpr int TILE = tile_elems<T>();
   constexpr int WPT = TILE / 32;  // allow words per warp tile
   constexpr uint32_t FULL = (1u << EPV) - 1u;
-  uint4* sfill = reinterpret_cast<uint4*>(smem);
-  uint8_t* sdead = smem + kFillBytes;
   const int32_t lane = threadIdx.x & 31;
-  const int32_t warp = threadIdx.x >> 5;
-  int32_t fill_first = INT_MAX;  // lowest index this thread wrote `fill` to
+  int32_t fill_first = INT_MAX;  // lowest index this lane wrote `fill` to
   VecArg va;
-  const uint4 fv = vec_splat<T>(fill);
-  const int32_t ntiles = (kVec && c1 > c0) ? (c1 - c0) / TILE : 0;
-  uint32_t* sbits = reinterpret_cast<uint32_t*>(
-      smem + kFillBytes + ((static_cast<size_t>(stream_tiles<T>(c1 - c0 > 0 ? c1 - c0 : 0)) + 15) &
-                           ~static_cast<size_t>(15)));
-  const int32_t w0 = c0 >> 5;
-  const int32_t nw = c1 > c0 ? ((c1 + 31) >> 5) - w0 : 0;
-  if (brow != nullptr) {
-    for (int32_t i = threadIdx.x; i < nw; i += kThreads) sbits[i] = __ldg(brow + w0 + i);
-  }
   if constexpr (kVec) {
-    for (int32_t i = threadIdx.x; i < kFillBytes / 16; i += kThreads) sfill[i] = fv;
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  }
-  __syncthreads();
-  int32_t vend = c0;
-  if constexpr (kVec) {
-    vend = c0 + ntiles * TILE;
-    for (int32_t ti = warp; ti < ntiles; ti += kWarps) {
-      const uint32_t w = (brow != nullptr && lane < WPT) ? sbits[ti * WPT + lane] : 0u;
-      const bool dead = !__any_sync(kAll, w != 0u);
-      if (lane == 0) sdead[ti] = dead ? 1 : 0;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      bool issued = false;
-      for (int32_t ti = 0; ti < ntiles;) {
-        if (!sdead[ti]) {
-          ++ti;
-          continue;
+    const int32_t ntiles = nt;
+    for (int32_t g0 = 0; g0 < ntiles; g0 += kGroupTiles) {
+      uint32_t w[kGroupTiles];
+#pragma unroll
+      for (int t = 0; t < kGroupTiles; ++t) {
+        w[t] = 0u;
+        if (brow != nullptr && g0 + t < ntiles && lane < WPT)
+          w[t] = __ldg(brow + ((e0 + (g0 + t) * tstep) >> 5) + lane);
+      }
+      uint32_t live = 0u;
+#pragma unroll
+      for (int t = 0; t < kGroupTiles; ++t)
+        live |= (__any_sync(kAll, w[t] != 0u) ? 1u : 0u) << t;
+      const int32_t ng = min(kGroupTiles, ntiles - g0);
+      const uint32_t dead = ((1u << ng) - 1u) & ~live;
+      if (dead != 0u && lane == 0) {
+        fill_first = min(fill_first, e0 + (g0 + __ffs(dead) - 1) * tstep);
+        uint32_t d = dead;
+        while (d != 0u) {
+          const int t0 = __ffs(d) - 1;
+          const int run = tstep == TILE ? __ffs(~(d >> t0)) - 1 : 1;
+          bulk_fill(row + e0 + (g0 + t0) * tstep,
+                    static_cast<uint32_t>(run * TILE * static_cast<int32_t>(sizeof(T))), sfill);
+          d &= ~(((1u << run) - 1u) << t0);
         }
-        int32_t te = ti + 1;
-        while (te < ntiles && sdead[te]) ++te;
-        bulk_fill(row + c0 + ti * TILE, static_cast<uint32_t>((te - ti) * TILE * sizeof(T)), sfill);
-        fill_first = min(fill_first, c0 + ti * TILE);
         issued = true;
-        ti = te;
       }
-      if (issued) {
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      }
-    }
-    for (int32_t ti = warp; ti < ntiles; ti += kWarps) {
-      if (sdead[ti]) continue;
-      const int32_t tb = c0 + ti * TILE;
-      const uint32_t w = (brow != nullptr && lane < WPT) ? sbits[ti * WPT + lane] : 0u;
-      uint32_t bits[kVPT];
 #pragma unroll
-      for (int j = 0; j < kVPT; ++j) {
-        const int v = lane + 32 * j;
-        const uint32_t word = __shfl_sync(kAll, w, (v * EPV) >> 5);
-        bits[j] = (word >> ((v * EPV) & 31)) & FULL;
-      }
-      uint4* base = reinterpret_cast<uint4*>(row + tb);
-      // Lanes of a warp see different bit patterns: every step below is the
-      // same instruction stream for all of them (predicated loads and store,
-      // branch-free blend), so a warp never runs the cases one after another.
-      // Soft vectors go in groups (logits + biases in flight together).
-      constexpr int G = kSoft ? (sizeof(Bits) == 4 ? 2 : 1) : kVPT;
-      constexpr int NB = kSoft ? G * (EPV / 4) : 1;
+      for (int t = 0; t < kGroupTiles; ++t) {
+        if (((live >> t) & 1u) == 0u) continue;  // the same for the whole warp
+        const int32_t tb = e0 + (g0 + t) * tstep;
+        uint32_t bits[kVPT];
 #pragma unroll
-      for (int g = 0; g < kVPT; g += G) {
-        uint4 val[G];
-        float4 bias[NB];
+        for (int j = 0; j < kVPT; ++j) {
+          const int v = lane + 32 * j;
+          const uint32_t word = __shfl_sync(kAll, w[t], (v * EPV) >> 5);
+          bits[j] = (word >> ((v * EPV) & 31)) & FULL;
+        }
+        uint4* base = reinterpret_cast<uint4*>(row + tb);
+        // soft vectors go in groups (logits + biases in flight together)
+        constexpr int G = kSoft ? (sizeof(Bits) == 4 ? 2 : 1) : kVPT;
+        constexpr int NB = kSoft ? G * (EPV / 4) : 1;
 #pragma unroll
-        for (int jj = 0; jj < G; ++jj) {
-          const int j = g + jj;
-          const bool need = (kArgmax || kSoft) ? (bits[j] != 0u)
-                                               : (bits[j] != 0u && bits[j] != FULL);
-          val[jj] = make_uint4(0u, 0u, 0u, 0u);  // not read by the blend unless loaded
-          if (need) val[jj] = __ldcs(base + lane + 32 * j);
-          if constexpr (kSoft) {
-            const float4* lb =
-                reinterpret_cast<const float4*>(lrow + tb + (lane + 32 * j) * EPV);
+        for (int g = 0; g < kVPT; g += G) {
+          uint4 val[G];
+          float4 bias[NB];
 #pragma unroll
-            for (int q = 0; q < EPV / 4; ++q) {
-              bias[jj * (EPV / 4) + q] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-              if (need) bias[jj * (EPV / 4) + q] = __ldg(lb + q);
+          for (int jj = 0; jj < G; ++jj) {
+            const int j = g + jj;
+            const bool need = (kArgmax || kSoft) ? (bits[j] != 0u)
+                                                 : (bits[j] != 0u && bits[j] != FULL);
+            val[jj] = make_uint4(0u, 0u, 0u, 0u);  // not read by the blend unless loaded
+            if (need) val[jj] = __ldcs(base + lane + 32 * j);
+            if constexpr (kSoft) {
+              const float4* lb =
+                  reinterpret_cast<const float4*>(lrow + tb + (lane + 32 * j) * EPV);
+#pragma unroll
+              for (int q = 0; q < EPV / 4; ++q) {
+                bias[jj * (EPV / 4) + q] =
+                    make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+                if (need) bias[jj * (EPV / 4) + q] = __ldg(lb + q);
+              }
             }
           }
-        }
 #pragma unroll
-        for (int jj = 0; jj < G; ++jj) {
-          const int j = g + jj;
-          uint4 out;
-          if constexpr (kSoft) {
-            out = soft_vec<T>(val[jj], &bias[jj * (EPV / 4)], alpha);
-          } else {
-            out = vec_blend<T>(val[jj], bits[j], fill);
+          for (int jj = 0; jj < G; ++jj) {
+            const int j = g + jj;
+            uint4 out;
+            if constexpr (kSoft) {
+              out = soft_vec<T>(val[jj], &bias[jj * (EPV / 4)], alpha);
+            } else {
+              out = vec_blend<T>(val[jj], bits[j], fill);
+            }
+            if (kSoft || bits[j] != FULL) __stcs(base + lane + 32 * j, out);
+            if constexpr (kArgmax)
+              vec_arg_fold(va, vec_max<T>(out), tb + (lane + 32 * j) * EPV);
           }
-          if (kSoft || bits[j] != FULL) __stcs(base + lane + 32 * j, out);
-          if constexpr (kArgmax) vec_arg_fold(va, vec_max<T>(out), tb + (lane + 32 * j) * EPV);
         }
       }
     }
+    if (issued) asm volatile("cp.async.bulk.commit_group;" ::: "memory");
   }
   Bits* rb = reinterpret_cast<Bits*>(row);
-  for (int32_t e = vend + static_cast<int32_t>(threadIdx.x); e < c1; e += kThreads) {
-    const bool allowed = brow != nullptr && ((sbits[(e >> 5) - w0] >> (e & 31)) & 1u);
+  for (int32_t e = s0 + lane; e < s1; e += 32) {
+    const bool allowed = brow != nullptr && ((__ldg(brow + (e >> 5)) >> (e & 31)) & 1u);
     if constexpr (kSoft) {
       const Bits y = soft_one<T>(rb[e], allowed ? __ldg(lrow + e) : -INFINITY, alpha);
       rb[e] = y;
@@ -323,7 +313,10 @@ __device__ __forceinline__ void mask_chunk(T* __restrict__ row, int32_t c0, int3
 }
 
 // ---------------------------------------------------------------------------
-// Kernels built on mask_chunk, shared by the dense and the PDA paths.
+// Kernels built on warp_span, shared by the dense, soft and PDA paths. A CTA
+// owns `chunk` elements of one row (kWarps equal spans, one per warp); the
+// hardware block scheduler hands CTAs of cheap and expensive rows out
+// dynamically.
 
 // What a row masks against: its allow words (nullptr = reject everything) and,
 // for the dense commit, its state and pool slot.
@@ -392,89 +385,143 @@ struct DenseCommit {
   }
 };
 
-// Register cap (resident CTAs per SM) and warp tiles per warp of one apply
-// CTA; tuned on B200 (8 resident CTAs beat fewer CTAs with more registers).
+// Register cap (resident CTAs per SM) and warp tiles per warp of a CTA;
+// tuned on B200 (8 resident CTAs beat fewer CTAs with more registers).
 #ifndef BPD_APPLY_MIN_BLOCKS
 #define BPD_APPLY_MIN_BLOCKS 8
-#endif
-#ifndef BPD_APPLY_TILES_PER_WARP
-#define BPD_APPLY_TILES_PER_WARP 4
 #endif
 #ifndef BPD_STEP_MIN_BLOCKS
 #define BPD_STEP_MIN_BLOCKS 8
 #endif
+#ifndef BPD_TILES_PER_WARP
+#define BPD_TILES_PER_WARP 4
+#endif
 
-// Mask only: one CTA per (row, segment); the hardware block scheduler hands
-// segments of cheap and expensive rows out dynamically.
+// Chunk of one CTA: `chunks_per_row` CTAs per row when the caller asks for
+// it, else BPD_TILES_PER_WARP warp tiles per warp. Always a multiple of
+// kWarps warp tiles, so every warp span starts on a tile.
+template <typename T>
+inline int32_t stream_chunk(int32_t V, int32_t chunks_per_row) {
+  constexpr int32_t UNIT = tile_elems<T>() * kWarps;
+  if (chunks_per_row <= 0) return UNIT * BPD_TILES_PER_WARP;
+  const int32_t per = (V + chunks_per_row - 1) / chunks_per_row;
+  return ((per + UNIT - 1) / UNIT) * UNIT;
+}
+
+// This warp's share of the CTA chunk [c0, c1): with the vector path, the
+// chunk's full tiles w, w + kWarps, ... (adjacent warps on adjacent tiles) and,
+// for the last warp, the ragged end; without it a contiguous element range.
+struct WarpShare {
+  int32_t e0, nt, tstep, s0, s1;
+};
+
+template <typename T, bool kVec>
+__device__ __forceinline__ WarpShare warp_share(int32_t c0, int32_t c1) {
+  constexpr int32_t TILE = tile_elems<T>();
+  const int32_t w = static_cast<int32_t>(threadIdx.x >> 5);
+  WarpShare r;
+  if constexpr (kVec) {
+    const int32_t ntc = c1 > c0 ? (c1 - c0) / TILE : 0;
+    r.e0 = c0 + w * TILE;
+    r.nt = ntc > w ? (ntc - w + kWarps - 1) / kWarps : 0;
+    r.tstep = kWarps * TILE;
+    r.s0 = c0 + ntc * TILE;
+    r.s1 = w == kWarps - 1 ? max(r.s0, c1) : r.s0;
+  } else {
+    const int32_t span = (c1 - c0 + kWarps - 1) / kWarps;
+    r.e0 = c0;
+    r.nt = 0;
+    r.tstep = TILE;
+    r.s0 = min(c1, c0 + w * span);
+    r.s1 = min(c1, r.s0 + span);
+  }
+  return r;
+}
+
+// Mask only: one CTA per (row, chunk).
 template <typename T, bool kVec, class Rows>
 __global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
     stream_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
                         typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  if constexpr (kVec) {
+    fill_init<T>(smem, fill);
+    __syncthreads();
+  }
   const int32_t row = blockIdx.x / chunks_per_row;
   const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
-  const int32_t c1 = min(V, c0 + chunk);
+  const WarpShare ws = warp_share<T, kVec>(c0, min(V, c0 + chunk));
   const RowInfo info = rows(row);
-  extern __shared__ __align__(16) uint8_t smem[];
   ArgState st;
-  mask_chunk<T, kVec, false, Rows::kSoft>(logits + row * row_stride, c0, c1, info.brow, fill, st,
-                                          smem, info.lrow, rows_alpha(rows));
+  bool issued = false;
+  warp_span<T, kVec, false, Rows::kSoft>(logits + row * row_stride, ws.e0, ws.nt, ws.tstep,
+                                         ws.s0, ws.s1, info.brow, fill,
+                                         reinterpret_cast<const uint4*>(smem), info.lrow,
+                                         rows_alpha(rows), st, issued);
+  if (issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
-// End of a fused step: reduce every thread's first-maximal element to the
-// CTA's, write it into rank 0's shared memory (distributed shared memory),
-// and after one cluster barrier let rank 0 commit the row's winning token.
-// All threads of every CTA of the cluster must call this.
-template <class Commit>
-__device__ __forceinline__ void cluster_commit(const ArgState& st, int32_t row,
-                                               const RowInfo& info, const Commit& commit) {
-  __shared__ uint64_t warp_best[kWarps];
-  __shared__ uint64_t cluster_best[8];
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int32_t k = static_cast<int32_t>(cluster.num_blocks());
-  const int32_t rank = static_cast<int32_t>(cluster.block_rank());
-  const uint64_t mine = warp_max_u64(pack_arg(st.key, st.idx));
-  const int32_t lane = threadIdx.x & 31;
-  const int32_t warp = threadIdx.x >> 5;
-  if (lane == 0) warp_best[warp] = mine;
-  __syncthreads();
-  if (warp == 0) {
-    uint64_t q = lane < kWarps ? warp_best[lane] : 0;
-    q = warp_max_u64(q);
-    if (lane == 0) {
-      uint64_t* dst = cluster.map_shared_rank(cluster_best, 0);
-      dst[rank] = q;
-    }
-  }
-  cluster.sync();
-  if (rank == 0 && threadIdx.x == 0) {
-    uint64_t best = 0;
-    for (int32_t r = 0; r < k; ++r) best = cluster_best[r] > best ? cluster_best[r] : best;
-    commit(row, info, unpack_idx(best));
-  }
+// Device scratch of the fused step: per row the best packed (key, ~index) so
+// far and the number of warps done. It must be zero before a launch; every
+// launch that runs to completion leaves it zero again (the row's last warp
+// clears it).
+struct StepScratch {
+  unsigned long long* best;  // [batch]
+  uint32_t* done;            // [batch]
+};
+
+constexpr size_t step_scratch_bytes(int32_t batch) {
+  return align256(sizeof(unsigned long long) * static_cast<size_t>(batch)) +
+         align256(sizeof(uint32_t) * static_cast<size_t>(batch));
 }
 
-// Fused greedy step: a thread-block cluster of `k` CTAs owns one row; every
-// CTA masks its slice and reduces its first-maximal element; the partials are
-// written into rank 0's shared memory (distributed shared memory), and after
-// one cluster barrier rank 0 hands the winning token to `commit`.
+inline StepScratch step_scratch_view(void* base, int32_t batch) {
+  char* p = static_cast<char*>(base);
+  StepScratch s;
+  s.best = reinterpret_cast<unsigned long long*>(p);
+  s.done = reinterpret_cast<uint32_t*>(
+      p + align256(sizeof(unsigned long long) * static_cast<size_t>(batch)));
+  return s;
+}
+
+// Fused greedy step: one CTA per (row, chunk), one span per warp. Each warp
+// masks its span and reduces its first-maximal element; the partials of a
+// row meet in one 64-bit atomicMax of the packed (key, ~index), and the warp
+// that finishes the row last (an atomic count after a fence -- the
+// last-block pattern, nothing ever waits) hands the winner to `commit`.
 template <typename T, bool kVec, class Rows, class Commit>
 __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
     stream_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
-                       Commit commit, typename Dt<T>::Bits fill, int32_t chunk) {
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int32_t k = static_cast<int32_t>(cluster.num_blocks());
-  const int32_t rank = static_cast<int32_t>(cluster.block_rank());
-  const int32_t row = blockIdx.x / k;
-  const int32_t c0 = rank * chunk;
-  const int32_t c1 = min(V, c0 + chunk);
-  const RowInfo info = rows(row);
+                       Commit commit, typename Dt<T>::Bits fill, int32_t chunk,
+                       int32_t chunks_per_row, StepScratch ws) {
   extern __shared__ __align__(16) uint8_t smem[];
+  if constexpr (kVec) {
+    fill_init<T>(smem, fill);
+    __syncthreads();
+  }
+  const int32_t row = blockIdx.x / chunks_per_row;
+  const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
+  const WarpShare sh = warp_share<T, kVec>(c0, min(V, c0 + chunk));
+  const RowInfo info = rows(row);
   ArgState st;
-  mask_chunk<T, kVec, true, Rows::kSoft>(logits + row * row_stride, c0, c1, info.brow, fill, st,
-                                         smem, info.lrow, rows_alpha(rows));
-  cluster_commit(st, row, info, commit);
+  bool issued = false;
+  warp_span<T, kVec, true, Rows::kSoft>(logits + row * row_stride, sh.e0, sh.nt, sh.tstep,
+                                        sh.s0, sh.s1, info.brow, fill,
+                                        reinterpret_cast<const uint4*>(smem), info.lrow,
+                                        rows_alpha(rows), st, issued);
+  const unsigned long long q = warp_max_u64(pack_arg(st.key, st.idx));
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(ws.best + row, q);
+    __threadfence();
+    const uint32_t parts = static_cast<uint32_t>(chunks_per_row * kWarps);
+    if (atomicAdd(ws.done + row, 1u) == parts - 1u) {
+      __threadfence();
+      const unsigned long long b = atomicExch(ws.best + row, 0ull);
+      ws.done[row] = 0u;
+      commit(row, info, unpack_idx(b));
+    }
+    if (issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  }
 }
 
 inline bool rows_aligned(const void* logits, int64_t row_stride, size_t esize) {
@@ -491,67 +538,45 @@ template <typename T, class Rows>
 bpd_status launch_stream_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
                                const Rows& rows, float neg_inf, cudaStream_t st,
                                const char* what) {
-  constexpr int TILE = tile_elems<T>();
-  const int32_t chunk = TILE * kWarps * BPD_APPLY_TILES_PER_WARP;
+  const int32_t chunk = stream_chunk<T>(V, 0);
   const int32_t chunks = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * chunks;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
   const auto fill = Dt<T>::from_float_host(neg_inf);
-  const size_t smem = stream_smem_bytes<T>(chunk);
   T* lg = static_cast<T*>(logits);
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    stream_apply_kernel<T, true, Rows><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
+    stream_apply_kernel<T, true, Rows><<<static_cast<unsigned>(grid), kThreads, kFillBytes, st>>>(
         lg, row_stride, V, rows, fill, chunk, chunks);
   } else {
-    stream_apply_kernel<T, false, Rows><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
+    stream_apply_kernel<T, false, Rows><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
         lg, row_stride, V, rows, fill, chunk, chunks);
   }
   return check_launch(what);
 }
 
-// CTAs per row of the fused step when the caller leaves it to us: aim for
-// ~1.5 waves of 8 resident CTAs on each of the 148 SMs.
-inline int32_t auto_ctas_per_row(int32_t batch) {
-  const int32_t want = (148 * 12 + batch - 1) / batch;
-  int32_t k = 1;
-  while (k < want && k < 8) k <<= 1;
-  return k;
-}
-
 template <typename T, class Rows, class Commit>
 bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, int32_t V,
-                              const Rows& rows, const Commit& commit, float neg_inf, int32_t k,
-                              cudaStream_t st, const char* what) {
-  constexpr int TILE = tile_elems<T>();
-  const int32_t per = (V + k - 1) / k;
-  const int32_t chunk = ((per + TILE - 1) / TILE) * TILE;
-  const int64_t grid = static_cast<int64_t>(batch) * k;
+                              const Rows& rows, const Commit& commit, float neg_inf,
+                              int32_t chunks_per_row, void* scratch, cudaStream_t st,
+                              const char* what) {
+  if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
+  if (!aligned16(scratch))
+    return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
+  const int32_t chunk = stream_chunk<T>(V, chunks_per_row);
+  const int32_t cpr = (V + chunk - 1) / chunk;
+  const int64_t grid = static_cast<int64_t>(batch) * cpr;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
   const auto fill = Dt<T>::from_float_host(neg_inf);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = stream_smem_bytes<T>(chunk);
-  if (cfg.dynamicSmemBytes > 48 * 1024)
-    return fail(BPD_ERR_INVALID, "%s: vocab too large for %d CTAs per row", what, k);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(k);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  const StepScratch ws = step_scratch_view(scratch, batch);
   T* lg = static_cast<T*>(logits);
-  cudaError_t e;
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    e = cudaLaunchKernelEx(&cfg, stream_step_kernel<T, true, Rows, Commit>, lg, row_stride, V,
-                           rows, commit, fill, chunk);
+    stream_step_kernel<T, true, Rows, Commit>
+        <<<static_cast<unsigned>(grid), kThreads, kFillBytes, st>>>(
+            lg, row_stride, V, rows, commit, fill, chunk, cpr, ws);
   } else {
-    e = cudaLaunchKernelEx(&cfg, stream_step_kernel<T, false, Rows, Commit>, lg, row_stride, V,
-                           rows, commit, fill, chunk);
+    stream_step_kernel<T, false, Rows, Commit><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+        lg, row_stride, V, rows, commit, fill, chunk, cpr, ws);
   }
-  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return check_launch(what);
 }
 

@@ -400,7 +400,7 @@ class CFGConstraintBatch:
         return status
 
     def step_greedy(self, seq_ids: Sequence[Hashable], logits: torch.Tensor,
-                    neg_inf: float = float("-inf"), ctas_per_row: int = 0) -> torch.Tensor:
+                    neg_inf: float = float("-inf"), chunks_per_row: int = 0) -> torch.Tensor:
         """NEW: ``apply_mask`` + ``logits.argmax(-1)`` + ``commit`` with the
         argmax fused into the masking pass. Masks ``logits`` in place, commits
         the first maximal token of every row and returns those tokens (int64);
@@ -419,7 +419,7 @@ class CFGConstraintBatch:
             C.byref(self.g._struct()), logits.data_ptr(), code, logits.stride(0),
             self._configs.data_ptr(), slots.data_ptr(), self._broken.view(torch.uint8).data_ptr(),
             B, mbuf.data_ptr(), cap, ws.data_ptr(), float(neg_inf), tokens.data_ptr(),
-            status.data_ptr(), int(ctas_per_row), _stream(logits)))
+            status.data_ptr(), int(chunks_per_row), _stream(logits)))
         self.last_status = status
         return tokens
 

@@ -467,13 +467,30 @@ def apply_soft_(
     return logits
 
 
+_SCRATCH: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def step_scratch(batch: int, device: torch.device) -> torch.Tensor:
+    """Zeroed device scratch of the fused steps for ``batch`` rows
+    (``bpd_step_scratch_bytes``), cached per device and grown on demand; the
+    kernels leave it zero, so one buffer serves every call on a stream."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, 0)
+    need = int(_capi.lib().bpd_step_scratch_bytes(max(int(batch), 1)))
+    buf = _SCRATCH.get(key)
+    if buf is None or buf.numel() < need:
+        buf = torch.zeros(need, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _SCRATCH[key] = buf
+    return buf
+
+
 def step_greedy_(
     logits: torch.Tensor,
     fsa: FsaTensors,
     state_pool: torch.Tensor,
     slots: torch.Tensor | None = None,
     neg_inf: float = float("-inf"),
-    ctas_per_row: int = 0,
+    chunks_per_row: int = 0,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """NEW, fused: mask ``logits`` in place, take the first maximal token of
     every masked row (``torch.argmax`` semantics) and commit it into
@@ -494,7 +511,8 @@ def step_greedy_(
     L.check(L.bpd_dense_step_greedy(
         logits.data_ptr(), code, logits.stride(0), B, fsa.vocab_size, state_pool.data_ptr(),
         _ptr(slots), bits.data_ptr(), bits.shape[1], tok_next.data_ptr(), fsa.num_states,
-        float(neg_inf), tokens.data_ptr(), nxt.data_ptr(), int(ctas_per_row), _stream(logits)))
+        float(neg_inf), tokens.data_ptr(), nxt.data_ptr(), int(chunks_per_row),
+        step_scratch(B, logits.device).data_ptr(), _stream(logits)))
     return tokens, nxt
 
 
@@ -504,7 +522,7 @@ def soft_step_greedy_(
     state_pool: torch.Tensor,
     slots: torch.Tensor | None = None,
     alpha: float = 1.0,
-    ctas_per_row: int = 0,
+    chunks_per_row: int = 0,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """NEW, fused: ``apply_soft_`` in place, the first maximal token of every
     biased row, and its commit into ``state_pool[slots[b]]``. Returns
@@ -527,13 +545,14 @@ def soft_step_greedy_(
     L.check(L.bpd_soft_step_greedy(
         logits.data_ptr(), code, logits.stride(0), B, fsa.vocab_size, state_pool.data_ptr(),
         _ptr(slots), la.data_ptr(), bits.data_ptr(), bits.shape[1], tok_next.data_ptr(),
-        fsa.num_states, float(alpha), tokens.data_ptr(), nxt.data_ptr(), int(ctas_per_row),
-        _stream(logits)))
+        fsa.num_states, float(alpha), tokens.data_ptr(), nxt.data_ptr(), int(chunks_per_row),
+        step_scratch(B, logits.device).data_ptr(), _stream(logits)))
     return tokens, nxt
 
 
 __all__ = [
     "DENSE_AUTO_LIMIT", "FsaTensors", "Vocabulary", "advance_state", "apply_mask_",
     "apply_soft_", "build_allow_bits", "build_lookahead", "build_token_transitions",
-    "compute_mask", "dfa_arrays", "soft_step_greedy_", "step_greedy_", "words_stride",
+    "compute_mask", "dfa_arrays", "soft_step_greedy_", "step_greedy_", "step_scratch",
+    "words_stride",
 ]

@@ -108,19 +108,26 @@ bpd_status bpd_dense_mask_bits(
     const uint32_t* allow_bits, int32_t words_stride, int32_t num_states,
     int32_t vocab_size, uint32_t* out_bits, void* stream);
 
+/* NEW. Device scratch of the fused steps (bpd_dense_step_greedy,
+ * bpd_soft_step_greedy) for up to `batch` rows: zero it once before the first
+ * call; every call that runs to completion leaves it zero again. One scratch
+ * per stream: calls that share it must not run concurrently. */
+size_t bpd_step_scratch_bytes(int32_t batch);
+
 /* NEW fused greedy step: apply_mask (as bpd_dense_apply_mask) + argmax of the
  * masked row (first maximal index, NaN counts as maximal, like torch.argmax)
  * + commit of that token (as bpd_dense_advance with write_back = 1).
  * token_out int64 [batch]; next_out int32 [batch] may be NULL.
- * ctas_per_row (0 = automatic, else 1, 2, 4 or 8) CTAs, one thread-block
- * cluster, share one row and reduce the argmax through distributed shared
- * memory. */
+ * A persistent grid takes (row, chunk) items from an atomic counter;
+ * chunks_per_row (0 = automatic, else 1..4096) sets how many items a row is
+ * cut into. step_scratch: bpd_step_scratch_bytes(batch) bytes, 16-byte
+ * aligned. */
 bpd_status bpd_dense_step_greedy(
     void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
     int32_t vocab_size, int32_t* state_pool, const int64_t* slots,
     const uint32_t* allow_bits, int32_t words_stride, const int32_t* tok_next,
     int32_t num_states, float neg_inf, int64_t* token_out, int32_t* next_out,
-    int32_t ctas_per_row, void* stream);
+    int32_t chunks_per_row, void* step_scratch, void* stream);
 
 /* --------------------------------------------------------------------------
  * Byte-walk path: the same ops on the raw symbol-class DFA, for automata
@@ -189,13 +196,15 @@ bpd_status bpd_soft_apply(
  * token of every row (torch.argmax order) into token_out (int64 [batch]) and
  * its commit next = tok_next[state, token] into state_pool[slots[b]] (and
  * next_out, may be NULL). Same results as apply_soft_ + argmax + commit
- * (batch.py:192-215) with one pass over the logits fewer. */
+ * (batch.py:192-215) with one pass over the logits fewer. chunks_per_row and
+ * step_scratch as in bpd_dense_step_greedy. */
 bpd_status bpd_soft_step_greedy(
     void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
     int32_t vocab_size, int32_t* state_pool, const int64_t* slots,
     const float* lookahead, const uint32_t* allow_bits, int32_t words_stride,
     const int32_t* tok_next, int32_t num_states, float alpha,
-    int64_t* token_out, int32_t* next_out, int32_t ctas_per_row, void* stream);
+    int64_t* token_out, int32_t* next_out, int32_t chunks_per_row,
+    void* step_scratch, void* stream);
 
 /* --------------------------------------------------------------------------
  * Pushdown automaton (context-free grammars)
@@ -262,12 +271,13 @@ bpd_status bpd_pda_apply_mask(
  * (int64 [batch]), then bpd_pda_advance of those tokens (broken / status_out
  * as there; broken may be NULL). Identical results to apply_mask + argmax +
  * commit (grammar/device.py:252-283) with one pass over the logits fewer.
- * ctas_per_row as in bpd_dense_step_greedy. */
+ * chunks_per_row as in bpd_dense_step_greedy; the step's scratch lives in
+ * the workspace (bpd_pda_workspace_bytes). */
 bpd_status bpd_pda_step_greedy(
     const bpd_pda_grammar* g, void* logits, int32_t dtype, int64_t row_stride,
     int32_t* config_pool, const int64_t* slots, uint8_t* broken, int32_t batch,
     void* memo, int32_t memo_capacity, void* workspace, float neg_inf,
-    int64_t* token_out, int32_t* status_out, int32_t ctas_per_row, void* stream);
+    int64_t* token_out, int32_t* status_out, int32_t chunks_per_row, void* stream);
 
 /* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64).
  * ok_out[b] (uint8, may be NULL) = 1 if the token was accepted; a rejected

@@ -35,7 +35,9 @@ def test_host_only_entry_points() -> None:
     assert L.bpd_dense_apply_mask(None, 0, 10, 1, 10, None, None, None, 1, 1, 0.0, None) == 1
     assert b"null pointer" in L.bpd_last_error()
     assert L.bpd_dense_step_greedy(None, 0, 10, 1, 10, None, None, None, 1, None, 1, 0.0, None,
-                                   None, 3, None) == 1
+                                   None, 3, None, None) == 1
+    assert L.bpd_step_scratch_bytes(1024) >= 12 * 1024
+    assert L.bpd_step_scratch_bytes(1024) % 256 == 0
 
 
 def test_header_compiles_as_c() -> None:

@@ -251,8 +251,10 @@ def test_config2_fused_step_equals_unfused_and_oracle(orc: Oracle) -> None:
                               nxt.cpu().numpy()[rows])
 
 
-@pytest.mark.parametrize("k", [1, 2, 4, 8])
-def test_step_cluster_sizes_agree(k: int) -> None:
+@pytest.mark.parametrize("k", [1, 2, 3, 7, 32])
+def test_step_chunkings_agree(k: int) -> None:
+    """Any cut of the rows into work items gives the unfused result, and the
+    step scratch is zero again after the launch."""
     from bpdecode_b200 import ops
 
     fsa = _ipv4_large(32_000)
@@ -266,9 +268,10 @@ def test_step_cluster_sizes_agree(k: int) -> None:
     want_next = ops.advance_state(fsa, pool0, want_tok)
     lb = logits.clone()
     pool = pool0.clone()
-    tok, nxt = ops.step_greedy_(lb, fsa, pool, ctas_per_row=k)
+    tok, nxt = ops.step_greedy_(lb, fsa, pool, chunks_per_row=k)
     assert torch.equal(lb, la) and torch.equal(tok, want_tok)
     assert torch.equal(nxt, want_next) and torch.equal(pool, want_next)
+    assert int(ops.step_scratch(B, lb.device).count_nonzero()) == 0
 
 
 def test_argmax_ties_nan_and_finite_fill() -> None:

@@ -260,7 +260,7 @@ def test_fused_step_equals_unfused(name: str) -> None:
         a.apply_mask(ids, la)
         tok = la.argmax(-1)
         st = a.commit(ids, tok)
-        tb = b.step_greedy(ids, lb, ctas_per_row=(1, 2, 4, 8)[step % 4])
+        tb = b.step_greedy(ids, lb, chunks_per_row=(1, 2, 5, 16)[step % 4])
         assert torch.equal(la, lb)
         assert torch.equal(tb, tok)
         assert torch.equal(b.last_status, st)

@@ -147,7 +147,7 @@ def test_apply_soft_vector_path_matches_fp32_formula(dtype: torch.dtype, V: int)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("ctas", [0, 1, 2, 8])
+@pytest.mark.parametrize("ctas", [0, 1, 3, 16])
 @pytest.mark.parametrize("V,pad", [(128_256, 0), (128_256, 64), (50_001, 3)])
 def test_soft_step_greedy_equals_unfused(dtype: torch.dtype, ctas: int, V: int,
                                          pad: int) -> None:
