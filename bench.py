@@ -255,34 +255,44 @@ def _config(world: int) -> dict:
 
 
 def run_profile_case(args: argparse.Namespace) -> None:
-    """Small fixed cases for ncu captures (no timing, no side measurements):
-    `dense` = the bench's fused dense step (1024 rows, bf16, 8 logits buffers
-    of 262 MB, larger than L2); `pda` = the config-4 PDA step (256 rows,
-    fp32); `soft` = the fused soft-lookahead step (1024 rows, fp32, k = 4).
-    Each runs --warmup steps, restarts the rows (dense, soft), then --steps
-    steps on cuda:0."""
+    """Small fixed cases for ncu captures (no timing, no side measurements).
+    `dense` = the bench's fused dense step and `soft` = the fused soft step
+    (k = 4, fp32 copy of the same logits): 1024 rows, and before step j of an
+    episode the bench's logits buffer j is regenerated into one working
+    buffer (262 MB bf16 / 525 MB fp32, larger than L2), so the rows follow the
+    bench's trajectory with a device footprint of about 1 GB. `pda` = the
+    config-4 PDA step (256 rows, fp32, 4 buffers). Each runs --warmup steps,
+    restarts the rows (dense, soft), then --steps steps on cuda:0."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     n = args.warmup + args.steps
-    ring = 8 if args.profile_case == "dense" else 4
     if args.profile_case in ("dense", "soft"):
         _, fsas, pats = build_workload(0, device)
-        if args.profile_case == "dense":
-            batch = make_batch(fsas, pats)
-            bufs = [gen_logits(0, i, device) for i in range(ring)]
-            step = batch.step_greedy
-        else:
+        soft = args.profile_case == "soft"
+        if soft:
             from dataclasses import replace
 
             from bpdecode_b200.ops import build_lookahead
 
-            soft = [replace(f, lookahead=build_lookahead(f, 4)) for f in fsas]
-            batch = make_batch(soft, pats)
-            bufs = [gen_logits(0, i, device).float() for i in range(ring)]
-
-            def step(ids, lg):
-                return batch.soft_step_greedy(ids, lg, 1.0)
+            fsas = [replace(f, lookahead=build_lookahead(f, 4)) for f in fsas]
+        batch = make_batch(fsas, pats)
         ids = list(range(ROWS_PER_GPU))
+        work = torch.empty(ROWS_PER_GPU, V, dtype=torch.float32 if soft else torch.bfloat16,
+                           device=device)
+
+        def step(j: int) -> None:
+            if soft:
+                work.copy_(gen_logits(0, j % EPISODE, device))
+                batch.soft_step_greedy(ids, work, 1.0)
+            else:
+                gen_logits(0, j % EPISODE, device, out=work)
+                batch.step_greedy(ids, work)
+
+        for i in range(args.warmup):
+            step(i)
+        batch.reset_many(ids)  # the captured steps start an episode, as in the bench
+        for i in range(args.steps):
+            step(i)
     else:
         from bpdecode_b200 import tables
         from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
@@ -296,18 +306,13 @@ def run_profile_case(args: argparse.Namespace) -> None:
             batch.add(i)
         bias = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
         bufs = []
-        for i in range(ring):
+        for i in range(4):
             gen = torch.Generator(device=device).manual_seed(40_000 + i)
             x = torch.randn(256, V, generator=gen, device=device)
             x[:, bias] += 3.0
             bufs.append(x)
-        step = batch.step_greedy
-    for i in range(args.warmup):
-        step(ids, bufs[i % ring])
-    if args.profile_case != "pda":
-        batch.reset_many(ids)  # the captured steps start an episode, as in the bench
-    for i in range(args.steps):
-        step(ids, bufs[i % ring])
+        for i in range(n):
+            batch.step_greedy(ids, bufs[i % 4])
     torch.cuda.synchronize()
     print(json.dumps({"profile_case": args.profile_case, "steps": n}), flush=True)
 
@@ -458,12 +463,28 @@ def main() -> None:
     shard.finish()
 
 
-def _pda_config4(device: torch.device, rank: int, steps: int = 256) -> dict:
-    """Recursive JSON-value grammar on the PDA path: 256 rows, V = 128,256,
-    fp32 logits N(0,1) + 3 on the { [ " , tokens, memo cleared at the start;
-    one step = CFGConstraintBatch.step_greedy (mask + argmax + commit). Step
-    latency from CUDA events, run eagerly from Python and replayed from CUDA
-    graphs (one graph per logits buffer, captured after a warm-up)."""
+def _step_events(n: int, before, step) -> list[float]:
+    """Per-step device time (µs) of `step(i)`, CUDA events right around it;
+    `before(i)` (untimed, same stream) prepares step i's input."""
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n)]
+    for i in range(n):
+        before(i)
+        ev[i][0].record()
+        step(i)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    return [x.elapsed_time(y) * 1000 for x, y in ev]
+
+
+def _pda_config4(device: torch.device, rank: int, steps: int = 512) -> dict:
+    """Recursive JSON-value grammar on the PDA path (config 4): 256 rows,
+    V = 128,256, fp32 logits N(0,1) + 3 on the { [ " , tokens, memo cleared at
+    the start, 512 steps; one step = CFGConstraintBatch.step_greedy (mask +
+    argmax + commit). Every step gets unmasked logits: one of 32 seeded
+    buffers is copied into the step's input before it (untimed). Step latency
+    from CUDA events around the step, run eagerly from Python and replayed
+    from CUDA graphs (one graph per input buffer, captured after warm-up)."""
     from bpdecode_b200 import tables
     from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
     from bpdecode_b200.workloads import BIASED, vocab_large
@@ -476,7 +497,7 @@ def _pda_config4(device: torch.device, rank: int, steps: int = 256) -> dict:
     for i in ids:
         batch.add(i)
     bias = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
-    ring = min(steps, 32)
+    ring = 32
     src = []
     for i in range(ring):
         gen = torch.Generator(device=device).manual_seed(rank * 7919 + 40_000 + i)
@@ -484,66 +505,61 @@ def _pda_config4(device: torch.device, rank: int, steps: int = 256) -> dict:
         x[:, bias] += 3.0
         src.append(x)
     bufs = [x.clone() for x in src]
-    # one untimed step loads the kernels and allocates the memo / workspace;
-    # then the memo is cleared and every row restarts for the cold step
-    batch.step_greedy(ids, bufs[0].clone())
-    g.clear_memo()
-    for i in ids:
-        batch.reset(i)
-    torch.cuda.synchronize()
-    first0 = torch.cuda.Event(enable_timing=True)
-    first1 = torch.cuda.Event(enable_timing=True)
-    first0.record()
+
+    def fresh(i: int) -> None:
+        bufs[i % ring].copy_(src[i % ring])
+
+    def restart() -> None:
+        g.clear_memo()
+        for r in ids:
+            batch.reset(r)
+
+    # one untimed step loads the kernels and allocates the memo / workspace
+    fresh(0)
     batch.step_greedy(ids, bufs[0])
-    first1.record()
-    torch.cuda.synchronize()
-    first = first0.elapsed_time(first1) * 1000
-    # eager: steps issued back to back from Python
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for i in range(steps):
-        batch.step_greedy(ids, bufs[i % ring])
-    b.record()
-    torch.cuda.synchronize()
-    eager_us = a.elapsed_time(b) * 1000 / steps
+    restart()
+    first = _step_events(1, fresh, lambda i: batch.step_greedy(ids, bufs[0]))[0]
+    restart()
+    eager = _step_events(steps, fresh, lambda i: batch.step_greedy(ids, bufs[i % ring]))
     # graphs: one captured step per buffer, replayed in sequence
-    graphs = []
+    restart()
     s = torch.cuda.Stream(device)
     s.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(s):
         for i in range(3):
+            fresh(i)
             batch.step_greedy(ids, bufs[i % ring])
     torch.cuda.current_stream(device).wait_stream(s)
+    graphs = []
     for i in range(ring):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr):
             batch.step_greedy(ids, bufs[i])
         graphs.append(gr)
+    restart()
     torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(steps)]
-    for i in range(steps):
-        ev[i][0].record()
-        graphs[i % ring].replay()
-        ev[i][1].record()
-    torch.cuda.synchronize()
-    us = sorted(x.elapsed_time(y) * 1000 for x, y in ev)
+    us = sorted(_step_events(steps, fresh, lambda i: graphs[i % ring].replay()))
     del graphs
+    broken = int(batch._broken.sum())
     return {"workload": "recursive JSON-value GBNF, PDA, 256 rows, V=128256, fp32 N(0,1) "
-                        f"+3 bias, memo cleared at start, {steps} steps (logits ring {ring})",
+                        f"+3 bias, memo cleared at start, {steps} steps, unmasked logits "
+                        "every step",
             "step": "CFGConstraintBatch.step_greedy (mask + argmax + commit)",
             "graph_step_us_median": us[len(us) // 2], "graph_step_us_p90": us[int(len(us) * 0.9)],
-            "eager_step_us": eager_us, "first_step_us_cold_memo": first,
-            "row_steps_per_s": B / (us[len(us) // 2] * 1e-6),
+            "eager_step_us_median": sorted(eager)[len(eager) // 2],
+            "first_step_us_cold_memo": first,
+            "row_steps_per_s": B / (us[len(us) // 2] * 1e-6), "broken_rows_at_end": broken,
             "note": "the bounded PDA saturates at init on this grammar (8 configs), as the "
                     "reference does; after the first steps every row's config-set hits the memo"}
 
 
-def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 64) -> dict:
+def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 128) -> dict:
     """Soft lookahead (horizon 4) over the 8-regex dense rows in fp32: table
-    build time, then per step apply_soft + argmax + commit (the reference's
-    sequence) and the fused soft step (one launch)."""
+    build time, then one 128-step generation from the start states timed per
+    step two ways -- apply_soft + argmax + commit (the reference's sequence)
+    and the fused soft step (one launch). apply_soft adds the bias in place,
+    so every step gets unbiased logits: one of 16 seeded buffers is copied
+    into the step's input before it (untimed)."""
     from dataclasses import replace
 
     from bpdecode_b200.batch import ConstraintBatch
@@ -554,42 +570,41 @@ def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 64
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
     ids = list(range(ROWS_PER_GPU))
-    ring = min(steps, 16)
-    bufs = [torch.randn(ROWS_PER_GPU, V, device=device,
-                        generator=torch.Generator(device=device).manual_seed(rank * 31 + i))
-            for i in range(ring)]
+    ring = 16
+    src = [torch.randn(ROWS_PER_GPU, V, device=device,
+                       generator=torch.Generator(device=device).manual_seed(rank * 31 + i))
+           for i in range(ring)]
+    work = torch.empty_like(src[0])
+
+    def fresh(i: int) -> None:
+        work.copy_(src[i % ring])
 
     def timed(step) -> float:
         batch = ConstraintBatch(soft, capacity=ROWS_PER_GPU)
         for i in ids:
             batch.add(i, grammar=pats[i])
         for i in range(3):
-            step(batch, bufs[i % ring])
-        torch.cuda.synchronize()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        for i in range(steps):
-            step(batch, bufs[i % ring])
-        b.record()
-        torch.cuda.synchronize()
-        return a.elapsed_time(b) / steps
+            fresh(i)
+            step(batch)
+        batch.reset_many(ids)
+        return statistics.fmean(_step_events(steps, fresh, lambda i: step(batch)))
 
-    def unfused(batch, lg) -> None:
-        batch.apply_soft(ids, lg, 1.0)
-        batch.commit(ids, lg.argmax(-1))
+    def unfused(batch) -> None:
+        batch.apply_soft(ids, work, 1.0)
+        batch.commit(ids, work.argmax(-1))
 
-    ms = timed(unfused)
-    ms_fused = timed(lambda batch, lg: batch.soft_step_greedy(ids, lg, 1.0))
+    us = timed(unfused)
+    us_fused = timed(lambda batch: batch.soft_step_greedy(ids, work, 1.0))
     logit_bytes = 2 * 4 * V * ROWS_PER_GPU
-    return {"workload": f"soft lookahead k=4, 8 regexes, {ROWS_PER_GPU} rows, V={V}, fp32",
+    return {"workload": f"soft lookahead k=4, 8 regexes, {ROWS_PER_GPU} rows, V={V}, fp32, "
+                        f"{steps}-step generation from the start states",
             "table_build_s": build_s,
-            "unfused_ms_per_step": ms, "unfused_row_steps_per_s": ROWS_PER_GPU / (ms / 1e3),
-            "fused_ms_per_step": ms_fused,
-            "fused_row_steps_per_s": ROWS_PER_GPU / (ms_fused / 1e3),
-            "fused_logits_gbs": logit_bytes / (ms_fused / 1e3) / 1e9,
-            "note": "logits read + written once per step (2 x 4 B x V per row); "
-                    "lookahead rows (sum of states x V x 4 B) stay L2-resident"}
+            "unfused_ms_per_step": us / 1e3, "unfused_row_steps_per_s": ROWS_PER_GPU / (us / 1e6),
+            "fused_ms_per_step": us_fused / 1e3,
+            "fused_row_steps_per_s": ROWS_PER_GPU / (us_fused / 1e6),
+            "fused_logits_gbs": logit_bytes / (us_fused / 1e6) / 1e9,
+            "note": "fused_logits_gbs counts the logits read + written once per step "
+                    "(2 x 4 B x V per row); rejected tiles are written without a read"}
 
 
 def _reference_torch_gpu(batch, bufs, ring, device) -> dict:

@@ -33,7 +33,8 @@
 // Per mask call (all on the caller's stream, no host sync):
 //   memset(dedup) -> lookup_kernel (memo probe, dedup, memo claim)
 //   -> first_byte_kernel -> compute_kernel (misses only; both exit at once when
-//   every row hit) -> apply, or the fused step (apply + argmax) -> advance.
+//   every row hit) -> apply, or the fused step (apply + argmax, and the warp
+//   that finishes a row advances its config-set by the winning token).
 #include <algorithm>
 #include <mutex>
 
@@ -359,19 +360,16 @@ __device__ __forceinline__ int64_t slot_of(const int64_t* slots, int32_t b) {
 // ---------------------------------------------------------------------------
 // Mask pipeline.
 
-constexpr int kLookupWarps = 4;
-
 // One warp per row: memo lookup and in-batch dedup. A row whose content is
 // neither in the memo nor already claimed by an equal row of this call
 // becomes a representative: it is appended to the representative list and
-// its first-byte table is cleared for first_byte_kernel.
-__global__ void __launch_bounds__(kLookupWarps * 32)
-    lookup_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
-                  const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
-                  int32_t batch, Memo memo, Work w) {
+// its first-byte table is cleared for the first-byte phase.
+__device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
+                                           const int32_t* __restrict__ pool,
+                                           const int64_t* __restrict__ slots,
+                                           const uint8_t* __restrict__ broken, int32_t b,
+                                           const Memo& memo, const Work& w) {
   const int lane = threadIdx.x & 31;
-  const int32_t b = blockIdx.x * kLookupWarps + (threadIdx.x >> 5);
-  if (b >= batch) return;
   const int64_t slot = slot_of(slots, b);
   if (broken && broken[slot]) {
     if (lane == 0) {
@@ -451,11 +449,11 @@ __global__ void __launch_bounds__(kLookupWarps * 32)
 // (representative, byte) item, items taken from a counter so the whole grid
 // works on however many representatives this call has (none: every warp
 // exits at once).
-__global__ void __launch_bounds__(kThreads)
-    first_byte_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
-                      const int64_t* __restrict__ slots, Work w) {
-  __shared__ int32_t scratch[kWarps][NCFG];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+__device__ __forceinline__ void first_byte_items(const bpd_pda_grammar& g,
+                                                 const int32_t* __restrict__ pool,
+                                                 const int64_t* __restrict__ slots,
+                                                 const Work& w, int32_t* scratch) {
+  const int lane = threadIdx.x & 31;
   const int32_t items = w.counters[0] * 256;
   for (;;) {
     int32_t item = 0;
@@ -465,7 +463,7 @@ __global__ void __launch_bounds__(kThreads)
     const int32_t b = w.reps[item >> 8];
     const int byte = item & 255;
     const int32_t* base = pool + slot_of(slots, b) * NCFG;
-    const bool ok = w_advance_byte<false>(g, base, scratch[warp], byte, lane);
+    const bool ok = w_advance_byte<false>(g, base, scratch, byte, lane);
     if (ok && lane == 0) atomicOr(w.first + static_cast<int64_t>(b) * 8 + (byte >> 5), 1u << (byte & 31));
   }
 }
@@ -482,12 +480,12 @@ constexpr int32_t kComputeChunk = kWarps * 32 * 4;  // tokens per compute item
 // tokens) pairs taken from a counter by a resident grid; each warp decides 32
 // tokens at a time (lane = token), walking only the ones whose first byte
 // survives and that are longer than one byte.
-__global__ void __launch_bounds__(kThreads)
-    compute_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
-                   const int64_t* __restrict__ slots, Memo memo, Work w) {
-  __shared__ int32_t buf[kWarps][2][NCFG];
-  __shared__ uint32_t first[8];
-  __shared__ int32_t s_item;
+__device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
+                                              const int32_t* __restrict__ pool,
+                                              const int64_t* __restrict__ slots,
+                                              const Memo& memo, const Work& w,
+                                              int32_t (*buf)[2][NCFG], uint32_t* first,
+                                              int32_t& s_item) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int32_t V = g.vocab_size;
   const int32_t chunks = (V + kComputeChunk - 1) / kComputeChunk;
@@ -549,6 +547,36 @@ __global__ void __launch_bounds__(kThreads)
       if (lane == 0) out[t0 >> 5] = word;
     }
   }
+}
+
+constexpr int kLookupWarps = 4;
+
+// The mask pipeline's kernels, in stream order after a memset of the call's
+// dedup table and counters: memo lookup and in-batch dedup (a warp per row),
+// first bytes of the representatives, their allow bits. With every row a
+// memo hit the last two find no items and end at once.
+__global__ void __launch_bounds__(kLookupWarps * 32)
+    lookup_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
+                  const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
+                  int32_t batch, Memo memo, Work w) {
+  const int32_t b = blockIdx.x * kLookupWarps + (threadIdx.x >> 5);
+  if (b < batch) lookup_row(g, pool, slots, broken, b, memo, w);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    first_byte_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
+                      const int64_t* __restrict__ slots, Work w) {
+  __shared__ int32_t scratch[kWarps][NCFG];
+  first_byte_items(g, pool, slots, w, scratch[threadIdx.x >> 5]);
+}
+
+__global__ void __launch_bounds__(kThreads)
+    compute_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
+                   const int64_t* __restrict__ slots, Memo memo, Work w) {
+  __shared__ int32_t buf[kWarps][2][NCFG];
+  __shared__ uint32_t first[8];
+  __shared__ int32_t s_item;
+  compute_items(g, pool, slots, memo, w, buf, first, s_item);
   // the last kernel of every mask call: the next call gets a new tag (the
   // lookups of this call, which read the old epoch, have all finished)
   if (memo.cap && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -576,11 +604,66 @@ struct PdaRows {
   }
 };
 
-// The fused PDA step's argmax only records the token; advance_kernel commits.
-struct TokenOut {
+// Advance config-set pool[slots[b]] by token t, one warp, with 3 * NCFG
+// int32 of shared memory: an exact trial walk of the token's bytes, written
+// back only if every byte is accepted; EOS never changes the config-set and
+// is accepted iff it is complete (pda_cpu.cpp:35-54). Then ok / broken /
+// status as grammar/device.py:268-283.
+__device__ __forceinline__ void warp_commit_token(const bpd_pda_grammar& g, int32_t* pool,
+                                                  int64_t slot, int32_t b, int64_t t,
+                                                  int32_t* buf, uint8_t* ok_out, uint8_t* broken,
+                                                  int32_t* status_out) {
+  const int lane = threadIdx.x & 31;
+  int32_t* row = pool + slot * NCFG;
+  int32_t* trial = buf;
+  w_copy(trial, row, lane);
+  bool ok;
+  if (t == g.eos_id) {
+    ok = is_complete(g, trial);  // EOS never changes the config-set
+  } else if (t < 0 || t >= g.vocab_size) {
+    ok = false;
+  } else {
+    const int32_t s = __ldg(g.tok_offsets + t), e = __ldg(g.tok_offsets + t + 1);
+    const int32_t* cur = trial;
+    int which = 1;
+    ok = true;
+    for (int32_t i = s; i < e && ok; ++i) {
+      int32_t* nxt = buf + which * NCFG;
+      ok = w_advance_byte<true>(g, cur, nxt, __ldg(g.tok_bytes + i), lane);
+      cur = nxt;
+      which = which == 1 ? 2 : 1;
+    }
+    if (ok && cur != trial) {
+      for (int k = lane; k < NCFG; k += 32) row[k] = cur[k];
+    }
+  }
+  if (lane == 0) {
+    if (ok_out) ok_out[b] = ok ? 1 : 0;
+    if (broken) {
+      const uint8_t br = static_cast<uint8_t>(broken[slot] | (ok ? 0 : 1));
+      broken[slot] = br;
+      if (status_out) status_out[b] = br ? -1 : 1;
+    } else if (status_out) {
+      status_out[b] = ok ? 1 : -1;
+    }
+  }
+}
+
+// Commit of the fused PDA step: record the token and advance the row's
+// config-set by it, in the warp that finished the row.
+struct PdaCommit {
+  static constexpr int kSmemBytes = 3 * NCFG * static_cast<int>(sizeof(int32_t));
+  bpd_pda_grammar g;
+  int32_t* pool;
+  const int64_t* slots;
   int64_t* token_out;
-  __device__ __forceinline__ void operator()(int32_t row, const RowInfo&, int32_t tok) const {
-    token_out[row] = tok;
+  uint8_t* broken;
+  int32_t* status_out;
+  __device__ __forceinline__ void operator()(int32_t row, const RowInfo&, int32_t tok,
+                                             uint8_t* smem) const {
+    if ((threadIdx.x & 31) == 0) token_out[row] = tok;
+    warp_commit_token(g, pool, slot_of(slots, row), row, tok, reinterpret_cast<int32_t*>(smem),
+                      nullptr, broken, status_out);
   }
 };
 
@@ -603,46 +686,13 @@ __global__ void __launch_bounds__(kAdvWarps * 32)
                    int32_t batch, const void* __restrict__ tokens, int32_t tokens64,
                    uint8_t* __restrict__ ok_out, uint8_t* __restrict__ broken,
                    int32_t* __restrict__ status_out) {
-  __shared__ int32_t buf[kAdvWarps][3][NCFG];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ int32_t buf[kAdvWarps][3 * NCFG];
+  const int warp = threadIdx.x >> 5;
   const int32_t b = blockIdx.x * kAdvWarps + warp;
   if (b >= batch) return;
-  const int64_t slot = slot_of(slots, b);
-  int32_t* row = pool + slot * NCFG;
   const int64_t t = tokens64 ? static_cast<const int64_t*>(tokens)[b]
                              : static_cast<int64_t>(static_cast<const int32_t*>(tokens)[b]);
-  int32_t* trial = buf[warp][0];
-  w_copy(trial, row, lane);
-  bool ok;
-  if (t == g.eos_id) {
-    ok = is_complete(g, trial);  // EOS never changes the config-set
-  } else if (t < 0 || t >= g.vocab_size) {
-    ok = false;
-  } else {
-    const int32_t s = __ldg(g.tok_offsets + t), e = __ldg(g.tok_offsets + t + 1);
-    const int32_t* cur = trial;
-    int which = 1;
-    ok = true;
-    for (int32_t i = s; i < e && ok; ++i) {
-      int32_t* nxt = buf[warp][which];
-      ok = w_advance_byte<true>(g, cur, nxt, __ldg(g.tok_bytes + i), lane);
-      cur = nxt;
-      which = which == 1 ? 2 : 1;
-    }
-    if (ok && cur != trial) {
-      for (int k = lane; k < NCFG; k += 32) row[k] = cur[k];
-    }
-  }
-  if (lane == 0) {
-    if (ok_out) ok_out[b] = ok ? 1 : 0;
-    if (broken) {
-      const uint8_t br = static_cast<uint8_t>(broken[slot] | (ok ? 0 : 1));
-      broken[slot] = br;
-      if (status_out) status_out[b] = br ? -1 : 1;
-    } else if (status_out) {
-      status_out[b] = ok ? 1 : -1;
-    }
-  }
+  warp_commit_token(g, pool, slot_of(slots, b), b, t, buf[warp], ok_out, broken, status_out);
 }
 
 // pda.hpp:200-207 on a zeroed struct (as the reference's pda_init op).
@@ -717,11 +767,10 @@ bpd_status launch_pda_apply(void* logits, int64_t row_stride, int32_t batch, int
 
 template <typename T>
 bpd_status launch_pda_step(void* logits, int64_t row_stride, int32_t batch, int32_t V,
-                           const Memo& memo, const Work& w, float neg_inf, int64_t* token_out,
-                           int32_t chunks_per_row, cudaStream_t st) {
-  return launch_stream_step<T, PdaRows, TokenOut>(logits, row_stride, batch, V, PdaRows{memo, w},
-                                                  TokenOut{token_out}, neg_inf, chunks_per_row,
-                                                  w.step, st,
+                           const Memo& memo, const Work& w, float neg_inf,
+                           const PdaCommit& commit, int32_t chunks_per_row, cudaStream_t st) {
+  return launch_stream_step<T, PdaRows, PdaCommit>(logits, row_stride, batch, V, PdaRows{memo, w},
+                                                   commit, neg_inf, chunks_per_row, w.step, st,
                                                   "pda step kernel");
 }
 
@@ -828,26 +877,20 @@ extern "C" bpd_status bpd_pda_step_greedy(
                                     workspace, &m, &w, st);
   if (rc) return rc;
   const int32_t k = chunks_per_row;
+  const PdaCommit commit{*g, config_pool, slots, token_out, broken, status_out};
   switch (dtype) {
     case BPD_F32:
-      rc = launch_pda_step<float>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
-                                  token_out, k, st);
-      break;
+      return launch_pda_step<float>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
+                                    commit, k, st);
     case BPD_BF16:
-      rc = launch_pda_step<__nv_bfloat16>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
-                                          token_out, k, st);
-      break;
+      return launch_pda_step<__nv_bfloat16>(logits, row_stride, batch, g->vocab_size, m, w,
+                                            neg_inf, commit, k, st);
     case BPD_F16:
-      rc = launch_pda_step<__half>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
-                                   token_out, k, st);
-      break;
+      return launch_pda_step<__half>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
+                                     commit, k, st);
     default:
       return fail(BPD_ERR_INVALID, "bpd_pda_step_greedy: unsupported logits dtype %d", dtype);
   }
-  if (rc) return rc;
-  advance_kernel<<<(batch + kAdvWarps - 1) / kAdvWarps, kAdvWarps * 32, 0, st>>>(
-      *g, config_pool, slots, batch, token_out, 1, nullptr, broken, status_out);
-  return check_launch("pda advance_kernel");
 }
 
 extern "C" bpd_status bpd_pda_advance(const bpd_pda_grammar* g, int32_t* config_pool,

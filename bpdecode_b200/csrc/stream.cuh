@@ -367,14 +367,19 @@ struct DenseRows {
 };
 
 // Dense commit of the chosen token: next = tok_next[state, token] (ops.py:301-306).
+// A Commit is called by all 32 lanes of the one warp that finishes a row,
+// with kSmemBytes of shared memory of its own.
 struct DenseCommit {
+  static constexpr int kSmemBytes = 0;
   int32_t* pool;
   const int32_t* tok_next;
   int32_t S;
   int32_t V;
   int64_t* token_out;
   int32_t* next_out;
-  __device__ __forceinline__ void operator()(int32_t row, const RowInfo& r, int32_t tok) const {
+  __device__ __forceinline__ void operator()(int32_t row, const RowInfo& r, int32_t tok,
+                                             uint8_t*) const {
+    if ((threadIdx.x & 31) != 0) return;
     const int32_t s = r.state;
     const int32_t next = (s >= 0 && s < S && tok >= 0 && tok < V)
                              ? tok_next[static_cast<int64_t>(s) * V + tok]
@@ -488,7 +493,8 @@ inline StepScratch step_scratch_view(void* base, int32_t batch) {
 // masks its span and reduces its first-maximal element; the partials of a
 // row meet in one 64-bit atomicMax of the packed (key, ~index), and the warp
 // that finishes the row last (an atomic count after a fence -- the
-// last-block pattern, nothing ever waits) hands the winner to `commit`.
+// last-block pattern, nothing ever waits) hands the winner to `commit`
+// (all its lanes, with Commit::kSmemBytes of shared memory).
 template <typename T, bool kVec, class Rows, class Commit>
 __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
     stream_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
@@ -510,7 +516,9 @@ __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
                                         reinterpret_cast<const uint4*>(smem), info.lrow,
                                         rows_alpha(rows), st, issued);
   const unsigned long long q = warp_max_u64(pack_arg(st.key, st.idx));
-  if ((threadIdx.x & 31) == 0) {
+  const int32_t lane = threadIdx.x & 31;
+  int32_t tok = -1;
+  if (lane == 0) {
     atomicMax(ws.best + row, q);
     __threadfence();
     const uint32_t parts = static_cast<uint32_t>(chunks_per_row * kWarps);
@@ -518,10 +526,12 @@ __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
       __threadfence();
       const unsigned long long b = atomicExch(ws.best + row, 0ull);
       ws.done[row] = 0u;
-      commit(row, info, unpack_idx(b));
+      tok = unpack_idx(b);
     }
     if (issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
+  tok = __shfl_sync(kAll, tok, 0);
+  if (tok >= 0) commit(row, info, tok, smem + kFillBytes);
 }
 
 inline bool rows_aligned(const void* logits, int64_t row_stride, size_t esize) {
@@ -569,12 +579,12 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   const auto fill = Dt<T>::from_float_host(neg_inf);
   const StepScratch ws = step_scratch_view(scratch, batch);
   T* lg = static_cast<T*>(logits);
+  const size_t smem = kFillBytes + Commit::kSmemBytes;
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    stream_step_kernel<T, true, Rows, Commit>
-        <<<static_cast<unsigned>(grid), kThreads, kFillBytes, st>>>(
-            lg, row_stride, V, rows, commit, fill, chunk, cpr, ws);
+    stream_step_kernel<T, true, Rows, Commit><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
+        lg, row_stride, V, rows, commit, fill, chunk, cpr, ws);
   } else {
-    stream_step_kernel<T, false, Rows, Commit><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
+    stream_step_kernel<T, false, Rows, Commit><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
         lg, row_stride, V, rows, commit, fill, chunk, cpr, ws);
   }
   return check_launch(what);
