@@ -183,6 +183,18 @@ class ConstraintBatch:
             mask_cache = MaskCache(self.fsa)
         self.cache: MaskCache | None = mask_cache or None
 
+    def add_grammar(self, fsa: FsaTensors) -> int:
+        """NEW: append a grammar to the batch and return its index for
+        :meth:`add`. States of the grammars already present keep their
+        global numbering (the new grammar's states are appended), so running
+        sequences are unaffected; the merged tables are rebuilt once."""
+        fsa = fsa.to(self.device)
+        if fsa.vocab_size != self._t.vocab_size:
+            raise ValueError("every grammar of a batch must share one vocabulary")
+        self.grammars.append(fsa)
+        self._t = _Tables(self.grammars)
+        return len(self.grammars) - 1
+
     # --- lifecycle -------------------------------------------------------
     def add(self, seq_id: Hashable, grammar: int = 0) -> int:
         if seq_id in self._slot_of:
@@ -220,6 +232,32 @@ class ConstraintBatch:
             if len(self._slot_cache) > self._SLOT_CACHE:
                 self._slot_cache.popitem(last=False)
         self._state.index_copy_(0, slots, starts)
+
+    # --- checkpoint / resume ------------------------------------------
+    def state_dict(self) -> dict:
+        """NEW: everything needed to resume the batch (host copies): the
+        per-slot automaton states and the slot / grammar bookkeeping. The
+        tables are not included -- restore into a batch built over the same
+        grammars (``torch.save`` / ``torch.load`` handle the dict)."""
+        return {"kind": "dense", "capacity": self.capacity,
+                "num_grammars": len(self.grammars),
+                "num_states": [g.num_states for g in self.grammars],
+                "state": self._state.cpu().clone(),
+                "slot_of": dict(self._slot_of), "grammar_of": dict(self._grammar_of),
+                "free": list(self._free)}
+
+    def load_state_dict(self, sd: dict) -> None:
+        """NEW: restore what :meth:`state_dict` saved (same capacity and
+        grammars), replacing every sequence of this batch."""
+        if sd.get("kind") != "dense" or sd["capacity"] != self.capacity:
+            raise ValueError("state_dict is not from a ConstraintBatch of this capacity")
+        if sd["num_states"] != [g.num_states for g in self.grammars]:
+            raise ValueError("state_dict was saved over different grammars")
+        self._state.copy_(sd["state"].to(device=self.device, dtype=torch.int32))
+        self._slot_of = dict(sd["slot_of"])
+        self._grammar_of = dict(sd["grammar_of"])
+        self._free = list(sd["free"])
+        self._slot_cache.clear()
 
     def __len__(self) -> int:
         return len(self._slot_of)

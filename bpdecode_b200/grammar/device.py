@@ -354,6 +354,28 @@ class CFGConstraintBatch:
         self._configs[slot] = self.g.init_config()
         self._broken[slot] = False
 
+    # --- checkpoint / resume ------------------------------------------
+    def state_dict(self) -> dict:
+        """NEW: the config-set pool ([capacity, 266] int32), the broken flags
+        and the slot bookkeeping, as host copies; the grammar tables and the
+        mask memo (a cache) are not included."""
+        return {"kind": "pda", "capacity": self.capacity, "num_states": self.g.num_states,
+                "configs": self._configs.cpu().clone(), "broken": self._broken.cpu().clone(),
+                "slot_of": dict(self._slot_of), "free": list(self._free)}
+
+    def load_state_dict(self, sd: dict) -> None:
+        """NEW: restore what :meth:`state_dict` saved (same capacity and
+        grammar), replacing every sequence of this batch."""
+        if sd.get("kind") != "pda" or sd["capacity"] != self.capacity:
+            raise ValueError("state_dict is not from a CFGConstraintBatch of this capacity")
+        if sd["num_states"] != self.g.num_states:
+            raise ValueError("state_dict was saved over a different grammar")
+        self._configs.copy_(sd["configs"].to(device=self.device, dtype=torch.int32))
+        self._broken.copy_(sd["broken"].to(device=self.device, dtype=torch.bool))
+        self._slot_of = dict(sd["slot_of"])
+        self._free = list(sd["free"])
+        self._slot_cache.clear()
+
     def __len__(self) -> int:
         return len(self._slot_of)
 
