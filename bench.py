@@ -261,7 +261,8 @@ def run_profile_case(args: argparse.Namespace) -> None:
     episode the bench's logits buffer j is regenerated into one working
     buffer (262 MB bf16 / 525 MB fp32, larger than L2), so the rows follow the
     bench's trajectory with a device footprint of about 1 GB. `pda` = the
-    config-4 PDA step (256 rows, fp32, 4 buffers). Each runs --warmup steps,
+    config-4 PDA step (256 rows, fp32, one of 4 seeded buffers copied into the
+    step's input each step). Each runs --warmup steps,
     restarts the rows (dense, soft), then --steps steps on cuda:0."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
@@ -305,14 +306,16 @@ def run_profile_case(args: argparse.Namespace) -> None:
         for i in ids:
             batch.add(i)
         bias = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
-        bufs = []
+        src = []
         for i in range(4):
             gen = torch.Generator(device=device).manual_seed(40_000 + i)
             x = torch.randn(256, V, generator=gen, device=device)
             x[:, bias] += 3.0
-            bufs.append(x)
+            src.append(x)
+        work = torch.empty_like(src[0])
         for i in range(n):
-            batch.step_greedy(ids, bufs[i % 4])
+            work.copy_(src[i % 4])  # unmasked logits every step
+            batch.step_greedy(ids, work)
     torch.cuda.synchronize()
     print(json.dumps({"profile_case": args.profile_case, "steps": n}), flush=True)
 
@@ -434,7 +437,8 @@ def main() -> None:
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "kernel": "dense_step_kernel (fused mask+argmax+commit)",
+                     "kernel": "stream_step_kernel<bf16, DenseRows, DenseCommit> (fused "
+                               "mask + argmax + commit)",
                      "kernel_ms": kern_ms,
                      "algo_bytes_per_row_step": ALGO_BYTES_PER_ROW_STEP},
         "clocks": clocks.summary(),
