@@ -254,6 +254,81 @@ def _config(world: int) -> dict:
     }
 
 
+def run_config5(args: argparse.Namespace) -> None:
+    """Config 5, per GPU: 1024 rows of continuous batching at V = 128,256 --
+    50 % regex requests (the 8 patterns), 30 % the JSON-Schema object (dense
+    DFA), 20 % the recursive JSON-value grammar (PDA); the dense rows are
+    scored with the horizon-4 soft lookahead on an fp32 copy of their bf16
+    logits, all rows greedy; every step 10 % of the requests are retired and
+    new ones admitted in their rows (bpdecode_b200.serving.MixedServingLoop).
+    Timed: --steps steps (default 1000), each = the fused steps of both paths
+    + the turnover, CUDA events around the whole loop (host bookkeeping
+    included), max over ranks."""
+    from bpdecode_b200 import shard, tables
+    from bpdecode_b200.grammar.device import PdaTensors
+    from bpdecode_b200.ops import FsaTensors
+    from bpdecode_b200.serving import MixedServingLoop
+    from bpdecode_b200.workloads import DENSE_PATTERNS, vocab_large
+
+    rank, world, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    shard.init("nccl", device)
+    vocab = vocab_large(V)
+    t0 = time.perf_counter()
+    dense = [FsaTensors.from_arrays(tables.load_dfa(n), vocab).to(device)
+             for n, _ in DENSE_PATTERNS]
+    dense.append(FsaTensors.from_arrays(tables.load_dfa("schema"), vocab).to(device))
+    dense = [f.with_lookahead(4) for f in dense]
+    pda = PdaTensors.from_arrays(tables.load_pda("jsonvalue"), vocab, device)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    loop = MixedServingLoop(ROWS_PER_GPU, dense, pda, n_regex=len(DENSE_PATTERNS),
+                            seed=rank * 7 + 1)
+    ring = 16
+    bufs = [gen_logits(rank, 20_000 + i, device) for i in range(ring)]
+    for i in range(args.warmup):
+        loop.step(bufs[i % ring])
+        loop.turnover()
+    torch.cuda.synchronize()
+    shard.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    steps = args.steps
+    with ClockSampler(local) as clocks:
+        a.record()
+        for i in range(steps):
+            loop.step(bufs[i % ring])
+            loop.turnover()
+        b.record()
+        torch.cuda.synchronize()
+    shard.barrier()
+    ms = shard.max_over_ranks([a.elapsed_time(b)], device)[0]
+    d_rows = int((loop.kind == 0).sum())
+    line = {
+        "metric": "constrained row-steps/sec (config 5 continuous batching)",
+        "value": ROWS_PER_GPU * world * steps / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "config 5: 1024 rows per GPU, V=128256, 50% regex (8 patterns) / "
+                               "30% JSON-Schema object (dense DFA) / 20% recursive JSON-value "
+                               "GBNF (PDA), soft lookahead k=4 fp32 on the dense rows, greedy, "
+                               "10% of requests retired and admitted every step",
+                   "rows_per_gpu": ROWS_PER_GPU, "global_batch": ROWS_PER_GPU * world,
+                   "parallelism": f"dp{world} (rows sharded by request, no collective)",
+                   "dense_rows_at_end": d_rows, "pda_rows_at_end": ROWS_PER_GPU - d_rows,
+                   "l2": f"{ring} logits buffers of 262 MB cycled (larger than L2)",
+                   "table_build_s": build_s},
+        "clocks": clocks.summary(),
+        "timing": "CUDA events around the whole loop, host bookkeeping of the turnover "
+                  "included; max over ranks",
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    shard.finish()
+
+
 def run_profile_case(args: argparse.Namespace) -> None:
     """Small fixed cases for ncu captures (no timing, no side measurements).
     `dense` = the bench's fused dense step and `soft` = the fused soft step
@@ -331,6 +406,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the PDA and soft-lookahead side measurements")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config5"],
+                    help="config2 (default, the headline line) or config5 (whole-box continuous "
+                         "batching: regex + schema + GBNF rows, soft lookahead, 10%% turnover)")
     ap.add_argument("--profile-case", choices=["dense", "pda", "soft"],
                     help="run a few untimed steps of one hot kernel for an ncu capture "
                          "(1 GPU, --warmup steps then --steps steps) and exit")
@@ -339,6 +417,9 @@ def main() -> None:
         ap.error("--warmup must be >= 3")
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.workload == "config5" and args.impl == "ours":
+        run_config5(args)
         return
     if args.impl == "reference":
         run_reference(args)
@@ -453,6 +534,7 @@ def main() -> None:
         del bufs
         torch.cuda.empty_cache()
         line["pda_config4"] = _pda_config4(device, rank)
+        line["dense_config3"] = _dense_config3(device, rank)
         line["soft_lookahead"] = _soft_lookahead(fsas, pats, device, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         off, tns, starts = 0, [], []
@@ -555,6 +637,48 @@ def _pda_config4(device: torch.device, rank: int, steps: int = 512) -> dict:
             "row_steps_per_s": B / (us[len(us) // 2] * 1e-6), "broken_rows_at_end": broken,
             "note": "the bounded PDA saturates at init on this grammar (8 configs), as the "
                     "reference does; after the first steps every row's config-set hits the memo"}
+
+
+def _dense_config3(device: torch.device, rank: int, steps: int = 256) -> dict:
+    """Config 3: the JSON-Schema object compiled to a dense DFA (1017 states),
+    V = 151,936, 512 rows, fp32 logits N(0, 1), greedy commit, 256 steps from
+    the start state; one step = ConstraintBatch.step_greedy. Every step gets
+    unmasked logits (one of 16 seeded buffers copied into its input, untimed);
+    CUDA events around each step."""
+    from bpdecode_b200 import tables
+    from bpdecode_b200.batch import ConstraintBatch
+    from bpdecode_b200.ops import FsaTensors
+    from bpdecode_b200.workloads import vocab_large
+
+    B3, V3 = 512, 151_936
+    fsa = FsaTensors.from_arrays(tables.load_dfa("schema"), vocab_large(V3)).to(device)
+    batch = ConstraintBatch(fsa, capacity=B3)
+    ids = list(range(B3))
+    for i in ids:
+        batch.add(i)
+    ring = 16
+    src = [torch.randn(B3, V3, device=device,
+                       generator=torch.Generator(device=device).manual_seed(rank * 131 + 7 + i))
+           for i in range(ring)]
+    work = torch.empty_like(src[0])
+
+    def fresh(i: int) -> None:
+        work.copy_(src[i % ring])
+
+    for i in range(3):
+        fresh(i)
+        batch.step_greedy(ids, work)
+    batch.reset_many(ids)
+    us = _step_events(steps, fresh, lambda i: batch.step_greedy(ids, work))
+    mean = statistics.fmean(us)
+    algo = 2 * V3 * 4 + 4 * ((V3 + 31) // 32) + 16
+    peak, _ = _peaks()
+    achieved = B3 * algo / (mean * 1e-6) / 1e9
+    return {"workload": "JSON-Schema object as a dense DFA (1017 states), V=151936, 512 rows, "
+                        "fp32 N(0,1), greedy, 256 steps from the start state",
+            "us_per_step": mean, "row_steps_per_s": B3 / (mean * 1e-6),
+            "algo_bytes_per_row_step": algo, "achieved_gbs": achieved,
+            "roofline_frac": achieved / peak}
 
 
 def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 128) -> dict:

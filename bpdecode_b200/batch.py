@@ -29,8 +29,11 @@ from . import _capi
 from .ops import (
     FsaTensors,
     _check_logits,
+    _ptr,
     _require_cuda,
+    _source_args,
     _stream,
+    _upload,
     _tokens,
     apply_mask_,
 )
@@ -218,6 +221,39 @@ class ConstraintBatch:
     def reset(self, seq_id: Hashable) -> None:
         self._state[self._slot_of[seq_id]] = self._t.starts[self._grammar_of[seq_id]]
 
+    def add_many(self, seq_ids: Sequence[Hashable], grammars: Sequence[int] | int = 0,
+                 ) -> list[int]:
+        """NEW: :meth:`add` of every id (grammar index per id, or one for
+        all) with one device write for the whole group."""
+        gs = [grammars] * len(seq_ids) if isinstance(grammars, int) else list(grammars)
+        if len(gs) != len(seq_ids) or len(set(seq_ids)) != len(seq_ids):
+            raise ValueError("add_many: one grammar per id, ids distinct")
+        if any(s in self._slot_of for s in seq_ids):
+            raise KeyError("add_many: a sequence is already in the batch")
+        if len(seq_ids) > len(self._free):
+            raise RuntimeError("ConstraintBatch is at capacity")
+        slots = [self._free.pop() for _ in seq_ids]
+        for sid, slot, g in zip(seq_ids, slots, gs):
+            self._slot_of[sid] = slot
+            self._grammar_of[sid] = g
+        if slots:
+            idx = _upload(slots, torch.int64, self.device)
+            val = _upload([self._t.starts[g] for g in gs], torch.int32, self.device)
+            self._state.index_copy_(0, idx, val)
+        self._slot_cache.clear()
+        return slots
+
+    def evict_many(self, seq_ids: Sequence[Hashable]) -> None:
+        """NEW: :meth:`evict` of every id with one device write."""
+        slots = [self._slot_of.pop(s) for s in seq_ids]
+        for s in seq_ids:
+            self._grammar_of.pop(s, None)
+        if slots:
+            idx = _upload(slots, torch.int64, self.device)
+            self._state.index_fill_(0, idx, FREE)
+        self._free.extend(slots)
+        self._slot_cache.clear()
+
     def reset_many(self, seq_ids: Sequence[Hashable]) -> None:
         """NEW: :meth:`reset` of every id in ``seq_ids`` as one device write on
         the current stream (no host synchronisation once the id list has been
@@ -226,8 +262,8 @@ class ConstraintBatch:
         key = ("starts",) + (seq_ids if isinstance(seq_ids, tuple) else tuple(seq_ids))
         starts = self._slot_cache.get(key)
         if starts is None:
-            starts = torch.tensor([self._t.starts[self._grammar_of[s]] for s in key[1:]],
-                                  dtype=torch.int32).to(self.device)
+            starts = _upload([self._t.starts[self._grammar_of[s]] for s in key[1:]],
+                             torch.int32, self.device)
             self._slot_cache[key] = starts
             if len(self._slot_cache) > self._SLOT_CACHE:
                 self._slot_cache.popitem(last=False)
@@ -272,8 +308,7 @@ class ConstraintBatch:
         if hit is not None:
             self._slot_cache.move_to_end(key)
             return hit
-        slots = torch.tensor([self._slot_of[s] for s in key], dtype=torch.int64)
-        slots = slots.to(self.device, non_blocking=False)
+        slots = _upload([self._slot_of[s] for s in key], torch.int64, self.device)
         self._slot_cache[key] = slots
         if len(self._slot_cache) > self._SLOT_CACHE:
             self._slot_cache.popitem(last=False)
@@ -391,6 +426,62 @@ class ConstraintBatch:
             t.allow_bits.shape[1], t.tok_next.data_ptr(), t.num_states, float(alpha),
             tokens.data_ptr(), None, int(chunks_per_row), self._scratch.data_ptr(),
             _stream(logits)))
+        return tokens
+
+    def step_greedy_from(
+        self,
+        seq_ids: Sequence[Hashable],
+        src: torch.Tensor,
+        src_rows: torch.Tensor | None = None,
+        out: torch.Tensor | None = None,
+        neg_inf: float = float("-inf"),
+        chunks_per_row: int = 0,
+    ) -> torch.Tensor:
+        """NEW: :meth:`step_greedy` on an fp32 working copy of the rows
+        without making the copy: row b reads ``src[src_rows[b]]`` (any float
+        dtype; rows 0..B-1 when ``src_rows`` is None), the masked fp32 row goes
+        to ``out[b]`` (None: nowhere), ``src`` is not modified. Returns the
+        tokens (int64)."""
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        t = self._t
+        code, rows, out = _source_args(src, t.vocab_size, B, src_rows, out, self.device)
+        tokens = torch.empty(B, dtype=torch.int64, device=self.device)
+        L = _capi.lib()
+        L.check(L.bpd_dense_step_greedy_from(
+            src.data_ptr(), code, src.stride(0), _ptr(rows), _ptr(out),
+            out.stride(0) if out is not None else 0, B, t.vocab_size, self._state.data_ptr(),
+            slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1],
+            t.tok_next.data_ptr(), t.num_states, float(neg_inf), tokens.data_ptr(), None,
+            int(chunks_per_row), self._scratch.data_ptr(), _stream(src)))
+        return tokens
+
+    def soft_step_greedy_from(
+        self,
+        seq_ids: Sequence[Hashable],
+        src: torch.Tensor,
+        src_rows: torch.Tensor | None = None,
+        out: torch.Tensor | None = None,
+        alpha: float = 1.0,
+        chunks_per_row: int = 0,
+    ) -> torch.Tensor:
+        """NEW: :meth:`soft_step_greedy` on an fp32 working copy of the rows
+        without making the copy (the contract of :meth:`step_greedy_from`)."""
+        t = self._t
+        if t.lookahead is None:
+            raise ValueError("fsa has no lookahead table; build with dense + with_lookahead")
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        code, rows, out = _source_args(src, t.vocab_size, B, src_rows, out, self.device)
+        tokens = torch.empty(B, dtype=torch.int64, device=self.device)
+        L = _capi.lib()
+        L.check(L.bpd_soft_step_greedy_from(
+            src.data_ptr(), code, src.stride(0), _ptr(rows), _ptr(out),
+            out.stride(0) if out is not None else 0, B, t.vocab_size, self._state.data_ptr(),
+            slots.data_ptr(), t.lookahead.data_ptr(), t.allow_bits.data_ptr(),
+            t.allow_bits.shape[1], t.tok_next.data_ptr(), t.num_states, float(alpha),
+            tokens.data_ptr(), None, int(chunks_per_row), self._scratch.data_ptr(),
+            _stream(src)))
         return tokens
 
     # --- queries ------------------------------------------------------

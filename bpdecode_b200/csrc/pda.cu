@@ -893,6 +893,49 @@ extern "C" bpd_status bpd_pda_step_greedy(
   }
 }
 
+extern "C" bpd_status bpd_pda_step_greedy_from(
+    const bpd_pda_grammar* g, const void* src, int32_t src_dtype, int64_t src_stride,
+    const int64_t* src_rows, float* out, int64_t out_stride, int32_t* config_pool,
+    const int64_t* slots, uint8_t* broken, int32_t batch, void* memo, int32_t memo_capacity,
+    void* workspace, float neg_inf, int64_t* token_out, int32_t* status_out,
+    int32_t chunks_per_row, void* stream) {
+  BPD_REQUIRE(batch >= 0, "bpd_pda_step_greedy_from: bad batch");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(src != nullptr && token_out != nullptr, "bpd_pda_step_greedy_from: null pointer");
+  BPD_REQUIRE(g && src_stride >= g->vocab_size &&
+                  (out == nullptr || out_stride >= g->vocab_size),
+              "bpd_pda_step_greedy_from: row stride < vocab");
+  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
+              "bpd_pda_step_greedy_from: chunks_per_row must be in [0, 4096]");
+  cudaStream_t st = as_stream(stream);
+  Memo m;
+  Work w;
+  bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
+                                    workspace, &m, &w, st);
+  if (rc) return rc;
+  const PdaCommit commit{*g, config_pool, slots, token_out, broken, status_out};
+  const PdaRows rows{m, w};
+  const int32_t V = g->vocab_size;
+  const char* what = "bpd_pda_step_greedy_from";
+  switch (src_dtype) {
+    case BPD_F32:
+      return launch_stream_step_src<float, PdaRows, PdaCommit>(
+          src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
+          chunks_per_row, w.step, st, what);
+    case BPD_BF16:
+      return launch_stream_step_src<__nv_bfloat16, PdaRows, PdaCommit>(
+          src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
+          chunks_per_row, w.step, st, what);
+    case BPD_F16:
+      return launch_stream_step_src<__half, PdaRows, PdaCommit>(
+          src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
+          chunks_per_row, w.step, st, what);
+    default:
+      return fail(BPD_ERR_INVALID, "bpd_pda_step_greedy_from: unsupported source dtype %d",
+                  src_dtype);
+  }
+}
+
 extern "C" bpd_status bpd_pda_advance(const bpd_pda_grammar* g, int32_t* config_pool,
                                       const int64_t* slots, int32_t batch, const void* tokens,
                                       int32_t tokens_int64, uint8_t* ok_out, uint8_t* broken,

@@ -239,3 +239,44 @@ extern "C" bpd_status bpd_soft_step_greedy(void* logits, int32_t dtype, int64_t 
       return fail(BPD_ERR_INVALID, "bpd_soft_step_greedy: unsupported logits dtype %d", dtype);
   }
 }
+
+extern "C" bpd_status bpd_soft_step_greedy_from(
+    const void* src, int32_t src_dtype, int64_t src_stride, const int64_t* src_rows,
+    float* out, int64_t out_stride, int32_t batch, int32_t vocab_size, int32_t* state_pool,
+    const int64_t* slots, const float* lookahead, const uint32_t* allow_bits,
+    int32_t words_stride, const int32_t* tok_next, int32_t num_states, float alpha,
+    int64_t* token_out, int32_t* next_out, int32_t chunks_per_row, void* step_scratch,
+    void* stream) {
+  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_soft_step_greedy_from: bad sizes");
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(src && state_pool && lookahead && allow_bits && tok_next && token_out,
+              "bpd_soft_step_greedy_from: null pointer");
+  BPD_REQUIRE(src_stride >= vocab_size && (out == nullptr || out_stride >= vocab_size),
+              "bpd_soft_step_greedy_from: row stride < vocab");
+  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
+              "bpd_soft_step_greedy_from: words_stride too small");
+  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
+              "bpd_soft_step_greedy_from: chunks_per_row must be in [0, 4096]");
+  cudaStream_t st = as_stream(stream);
+  const SoftRows rows{state_pool, slots, allow_bits, words_stride, lookahead, num_states,
+                      vocab_size, alpha};
+  const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
+  const char* what = "bpd_soft_step_greedy_from";
+  switch (src_dtype) {
+    case BPD_F32:
+      return launch_stream_step_src<float, SoftRows, DenseCommit>(
+          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
+          chunks_per_row, step_scratch, st, what);
+    case BPD_BF16:
+      return launch_stream_step_src<__nv_bfloat16, SoftRows, DenseCommit>(
+          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
+          chunks_per_row, step_scratch, st, what);
+    case BPD_F16:
+      return launch_stream_step_src<__half, SoftRows, DenseCommit>(
+          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
+          chunks_per_row, step_scratch, st, what);
+    default:
+      return fail(BPD_ERR_INVALID, "bpd_soft_step_greedy_from: unsupported source dtype %d",
+                  src_dtype);
+  }
+}

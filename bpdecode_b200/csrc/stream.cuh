@@ -85,12 +85,11 @@ __device__ __forceinline__ void vec_arg_fold(VecArg& a, float m, int32_t e0) {
   a.vec = take ? e0 : a.vec;
 }
 
-// Merge the winning vector's first maximal element into `st`. The vector is
-// read back from `row`: this thread wrote it (or left it untouched) itself.
+// Merge the winning vector's first maximal element into `st`; `v` is that
+// vector's value (read back, or computed again, by the thread that folded it).
 template <typename T>
-__device__ __forceinline__ void vec_arg_resolve(ArgState& st, const VecArg& a, const T* row) {
+__device__ __forceinline__ void vec_arg_resolve(ArgState& st, const VecArg& a, const uint4& v) {
   if (a.vec == INT_MAX) return;
-  const uint4 v = *reinterpret_cast<const uint4*>(row + a.vec);
   const uint32_t k = order_key(a.best);
   int32_t first = 0;
 #pragma unroll
@@ -163,6 +162,39 @@ __device__ __forceinline__ void bulk_fill(void* dst, uint32_t bytes, const uint4
 // Warp tiles whose allow words a warp loads at once.
 constexpr int kGroupTiles = 4;
 
+// The 16-byte vector of working type T at element e0 of a source row of type
+// S: the same bits when S == T, else (T = float) EPV elements of S widened.
+template <typename T, typename S>
+__device__ __forceinline__ uint4 load_src(const S* __restrict__ srow, int32_t e0) {
+  if constexpr (std::is_same_v<S, T>) {
+    return __ldcs(reinterpret_cast<const uint4*>(srow + e0));
+  } else {
+    static_assert(std::is_same_v<T, float> && sizeof(S) == 2, "fp32 from 16-bit sources");
+    const uint2 h = __ldcs(reinterpret_cast<const uint2*>(srow + e0));
+    if constexpr (std::is_same_v<S, __nv_bfloat16>) {
+      return make_uint4(h.x << 16, h.x & 0xFFFF0000u, h.y << 16, h.y & 0xFFFF0000u);
+    } else {
+      return make_uint4(__float_as_uint(__half2float(__ushort_as_half(h.x & 0xFFFFu))),
+                        __float_as_uint(__half2float(__ushort_as_half(h.x >> 16))),
+                        __float_as_uint(__half2float(__ushort_as_half(h.y & 0xFFFFu))),
+                        __float_as_uint(__half2float(__ushort_as_half(h.y >> 16))));
+    }
+  }
+}
+
+// Element e of a source row as working-type bits.
+template <typename T, typename S>
+__device__ __forceinline__ typename Dt<T>::Bits load_src_one(const S* srow, int32_t e) {
+  if constexpr (std::is_same_v<S, T>) {
+    return reinterpret_cast<const typename Dt<T>::Bits*>(srow)[e];
+  } else {
+    const uint16_t b = reinterpret_cast<const uint16_t*>(srow)[e];
+    return __float_as_uint(std::is_same_v<S, __nv_bfloat16>
+                               ? __uint_as_float(uint32_t(b) << 16)
+                               : __half2float(__ushort_as_half(b)));
+  }
+}
+
 // One warp masks [e0, e1) of `row` (e0 a multiple of the warp tile, so allow
 // words line up) against allow row `brow` (nullptr = reject everything); no
 // barrier, no shared state with the CTA's other warps except the read-only
@@ -194,8 +226,14 @@ constexpr int kGroupTiles = 4;
 // The warp's tiles start at e0 + i * tstep (i < nt; tstep = TILE: one
 // contiguous span, whose dead tiles merge into runs), then it handles the
 // scalar elements [s0, s1) one per lane.
-template <typename T, bool kVec, bool kArgmax, bool kSoft>
-__device__ __forceinline__ void warp_span(T* __restrict__ row, int32_t e0, int32_t nt,
+//
+// Source and destination: the values come from `srow` (type S) and the
+// result goes to `row` (working type T). In place (kInPlace: the same row)
+// all-allowed vectors are not written; otherwise every vector of `row` is,
+// and `row` may be nullptr: nothing is written (only the argmax is wanted).
+template <typename T, typename S, bool kInPlace, bool kVec, bool kArgmax, bool kSoft>
+__device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restrict__ srow,
+                                          int32_t e0, int32_t nt,
                                           int32_t tstep, int32_t s0, int32_t s1,
                                           const uint32_t* __restrict__ brow,
                                           typename Dt<T>::Bits fill, const uint4* sfill,
@@ -227,7 +265,7 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, int32_t e0, int32
       const uint32_t dead = ((1u << ng) - 1u) & ~live;
       if (dead != 0u && lane == 0) {
         fill_first = min(fill_first, e0 + (g0 + __ffs(dead) - 1) * tstep);
-        uint32_t d = dead;
+        uint32_t d = row != nullptr ? dead : 0u;
         while (d != 0u) {
           const int t0 = __ffs(d) - 1;
           const int run = tstep == TILE ? __ffs(~(d >> t0)) - 1 : 1;
@@ -235,7 +273,7 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, int32_t e0, int32
                     static_cast<uint32_t>(run * TILE * static_cast<int32_t>(sizeof(T))), sfill);
           d &= ~(((1u << run) - 1u) << t0);
         }
-        issued = true;
+        issued = issued || row != nullptr;
       }
 #pragma unroll
       for (int t = 0; t < kGroupTiles; ++t) {
@@ -259,10 +297,11 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, int32_t e0, int32
 #pragma unroll
           for (int jj = 0; jj < G; ++jj) {
             const int j = g + jj;
-            const bool need = (kArgmax || kSoft) ? (bits[j] != 0u)
-                                                 : (bits[j] != 0u && bits[j] != FULL);
+            const bool need = (kArgmax || kSoft || !kInPlace)
+                                  ? (bits[j] != 0u)
+                                  : (bits[j] != 0u && bits[j] != FULL);
             val[jj] = make_uint4(0u, 0u, 0u, 0u);  // not read by the blend unless loaded
-            if (need) val[jj] = __ldcs(base + lane + 32 * j);
+            if (need) val[jj] = load_src<T, S>(srow, tb + (lane + 32 * j) * EPV);
             if constexpr (kSoft) {
               const float4* lb =
                   reinterpret_cast<const float4*>(lrow + tb + (lane + 32 * j) * EPV);
@@ -283,7 +322,8 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, int32_t e0, int32
             } else {
               out = vec_blend<T>(val[jj], bits[j], fill);
             }
-            if (kSoft || bits[j] != FULL) __stcs(base + lane + 32 * j, out);
+            if (row != nullptr && (kSoft || !kInPlace || bits[j] != FULL))
+              __stcs(base + lane + 32 * j, out);
             if constexpr (kArgmax)
               vec_arg_fold(va, vec_max<T>(out), tb + (lane + 32 * j) * EPV);
           }
@@ -296,18 +336,42 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, int32_t e0, int32
   for (int32_t e = s0 + lane; e < s1; e += 32) {
     const bool allowed = brow != nullptr && ((__ldg(brow + (e >> 5)) >> (e & 31)) & 1u);
     if constexpr (kSoft) {
-      const Bits y = soft_one<T>(rb[e], allowed ? __ldg(lrow + e) : -INFINITY, alpha);
-      rb[e] = y;
+      const Bits y =
+          soft_one<T>(load_src_one<T, S>(srow, e), allowed ? __ldg(lrow + e) : -INFINITY, alpha);
+      if (rb != nullptr) rb[e] = y;
       if constexpr (kArgmax) arg_elem(st, Dt<T>::to_float(y), e);
     } else if (allowed) {
-      if constexpr (kArgmax) arg_elem(st, Dt<T>::to_float(rb[e]), e);
+      const Bits x = load_src_one<T, S>(srow, e);
+      if (!kInPlace && rb != nullptr) rb[e] = x;
+      if constexpr (kArgmax) arg_elem(st, Dt<T>::to_float(x), e);
     } else {
-      rb[e] = fill;
+      if (rb != nullptr) rb[e] = fill;
       fill_first = min(fill_first, e);
     }
   }
   if constexpr (kArgmax) {
-    vec_arg_resolve<T>(st, va, row);
+    if (va.vec != INT_MAX) {
+      // the winning vector: read back what this lane stored, or compute it
+      // again from the source when nothing was stored
+      uint4 v;
+      if (row != nullptr) {
+        v = *reinterpret_cast<const uint4*>(row + va.vec);
+      } else {
+        const uint32_t wd = brow != nullptr ? __ldg(brow + (va.vec >> 5)) : 0u;
+        const uint32_t bits = (wd >> (va.vec & 31)) & FULL;
+        const uint4 x = load_src<T, S>(srow, va.vec);
+        if constexpr (kSoft) {
+          float4 b[EPV / 4];
+#pragma unroll
+          for (int q = 0; q < EPV / 4; ++q)
+            b[q] = __ldg(reinterpret_cast<const float4*>(lrow + va.vec) + q);
+          v = soft_vec<T>(x, b, alpha);
+        } else {
+          v = vec_blend<T>(x, bits, fill);
+        }
+      }
+      vec_arg_resolve<T>(st, va, v);
+    }
     if (fill_first != INT_MAX) arg_elem(st, Dt<T>::to_float(fill), fill_first);
   }
 }
@@ -459,10 +523,11 @@ __global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
   const RowInfo info = rows(row);
   ArgState st;
   bool issued = false;
-  warp_span<T, kVec, false, Rows::kSoft>(logits + row * row_stride, ws.e0, ws.nt, ws.tstep,
-                                         ws.s0, ws.s1, info.brow, fill,
-                                         reinterpret_cast<const uint4*>(smem), info.lrow,
-                                         rows_alpha(rows), st, issued);
+  T* rowp = logits + row * row_stride;
+  warp_span<T, T, true, kVec, false, Rows::kSoft>(rowp, rowp, ws.e0, ws.nt, ws.tstep, ws.s0,
+                                                  ws.s1, info.brow, fill,
+                                                  reinterpret_cast<const uint4*>(smem), info.lrow,
+                                                  rows_alpha(rows), st, issued);
   if (issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
@@ -495,10 +560,16 @@ inline StepScratch step_scratch_view(void* base, int32_t batch) {
 // that finishes the row last (an atomic count after a fence -- the
 // last-block pattern, nothing ever waits) hands the winner to `commit`
 // (all its lanes, with Commit::kSmemBytes of shared memory).
-template <typename T, bool kVec, class Rows, class Commit>
+//
+// In place (S == T, kInPlace) the row is `logits` row `row`. Otherwise the
+// values come from source row `src_rows[row]` (row `row` when nullptr) of
+// `src` (type S) and the result goes to row `row` of `logits` (working type
+// T), or nowhere when `logits` is nullptr.
+template <typename T, typename S, bool kInPlace, bool kVec, class Rows, class Commit>
 __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
-    stream_step_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
-                       Commit commit, typename Dt<T>::Bits fill, int32_t chunk,
+    stream_step_kernel(T* __restrict__ logits, int64_t row_stride, const S* __restrict__ src,
+                       int64_t src_stride, const int64_t* __restrict__ src_rows, int32_t V,
+                       Rows rows, Commit commit, typename Dt<T>::Bits fill, int32_t chunk,
                        int32_t chunks_per_row, StepScratch ws) {
   extern __shared__ __align__(16) uint8_t smem[];
   if constexpr (kVec) {
@@ -511,10 +582,17 @@ __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
   const RowInfo info = rows(row);
   ArgState st;
   bool issued = false;
-  warp_span<T, kVec, true, Rows::kSoft>(logits + row * row_stride, sh.e0, sh.nt, sh.tstep,
-                                        sh.s0, sh.s1, info.brow, fill,
-                                        reinterpret_cast<const uint4*>(smem), info.lrow,
-                                        rows_alpha(rows), st, issued);
+  T* rowp = logits != nullptr ? logits + row * row_stride : nullptr;
+  const S* srow;
+  if constexpr (kInPlace) {
+    srow = rowp;
+  } else {
+    srow = src + (src_rows != nullptr ? src_rows[row] : static_cast<int64_t>(row)) * src_stride;
+  }
+  warp_span<T, S, kInPlace, kVec, true, Rows::kSoft>(rowp, srow, sh.e0, sh.nt, sh.tstep, sh.s0,
+                                                     sh.s1, info.brow, fill,
+                                                     reinterpret_cast<const uint4*>(smem),
+                                                     info.lrow, rows_alpha(rows), st, issued);
   const unsigned long long q = warp_max_u64(pack_arg(st.key, st.idx));
   const int32_t lane = threadIdx.x & 31;
   int32_t tok = -1;
@@ -581,11 +659,52 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   T* lg = static_cast<T*>(logits);
   const size_t smem = kFillBytes + Commit::kSmemBytes;
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    stream_step_kernel<T, true, Rows, Commit><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
-        lg, row_stride, V, rows, commit, fill, chunk, cpr, ws);
+    stream_step_kernel<T, T, true, true, Rows, Commit>
+        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(lg, row_stride, lg, row_stride,
+                                                               nullptr, V, rows, commit, fill,
+                                                               chunk, cpr, ws);
   } else {
-    stream_step_kernel<T, false, Rows, Commit><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
-        lg, row_stride, V, rows, commit, fill, chunk, cpr, ws);
+    stream_step_kernel<T, T, true, false, Rows, Commit>
+        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(lg, row_stride, lg, row_stride,
+                                                               nullptr, V, rows, commit, fill,
+                                                               chunk, cpr, ws);
+  }
+  return check_launch(what);
+}
+
+// The fused step on fp32 working values read from a source of type S
+// (gathered through `src_rows`, may be nullptr), written to `out` (fp32,
+// may be nullptr: tokens and commits only).
+template <typename S, class Rows, class Commit>
+bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int64_t* src_rows,
+                                  float* out, int64_t out_stride, int32_t batch, int32_t V,
+                                  const Rows& rows, const Commit& commit, float neg_inf,
+                                  int32_t chunks_per_row, void* scratch, cudaStream_t st,
+                                  const char* what) {
+  if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
+  if (!aligned16(scratch))
+    return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
+  const int32_t chunk = stream_chunk<float>(V, chunks_per_row);
+  const int32_t cpr = (V + chunk - 1) / chunk;
+  const int64_t grid = static_cast<int64_t>(batch) * cpr;
+  if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
+  const auto fill = Dt<float>::from_float_host(neg_inf);
+  const StepScratch ws = step_scratch_view(scratch, batch);
+  const size_t smem = kFillBytes + Commit::kSmemBytes;
+  const bool vec = rows_aligned(src, src_stride, sizeof(S)) &&
+                   (out == nullptr || rows_aligned(out, out_stride, sizeof(float))) &&
+                   (!Rows::kSoft || V % 4 == 0);
+  const S* sp = static_cast<const S*>(src);
+  if (vec) {
+    stream_step_kernel<float, S, false, true, Rows, Commit>
+        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(out, out_stride, sp, src_stride,
+                                                               src_rows, V, rows, commit, fill,
+                                                               chunk, cpr, ws);
+  } else {
+    stream_step_kernel<float, S, false, false, Rows, Commit>
+        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(out, out_stride, sp, src_stride,
+                                                               src_rows, V, rows, commit, fill,
+                                                               chunk, cpr, ws);
   }
   return check_launch(what);
 }

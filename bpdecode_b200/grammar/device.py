@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from .. import _capi
-from ..ops import _check_logits, _require_cuda, _stream, _tokens
+from ..ops import _check_logits, _require_cuda, _stream, _tokens, _upload
 from ..tokenizer import as_vocabulary
 
 # Must match the C ABI (BPD_PDA_MAX_CONFIGS / BPD_PDA_MAX_DEPTH / ..._INTS) and
@@ -354,6 +354,28 @@ class CFGConstraintBatch:
         self._configs[slot] = self.g.init_config()
         self._broken[slot] = False
 
+    def add_many(self, seq_ids: Sequence[Hashable]) -> list[int]:
+        """NEW: :meth:`add` of every id with one device write per pool."""
+        if len(set(seq_ids)) != len(seq_ids) or any(s in self._slot_of for s in seq_ids):
+            raise KeyError("add_many: ids must be distinct and new")
+        if len(seq_ids) > len(self._free):
+            raise RuntimeError("CFGConstraintBatch is at capacity")
+        slots = [self._free.pop() for _ in seq_ids]
+        for sid, slot in zip(seq_ids, slots):
+            self._slot_of[sid] = slot
+        if slots:
+            idx = _upload(slots, torch.int64, self.device)
+            self._configs.index_copy_(0, idx, self.g.init_batch(len(slots)))
+            self._broken.index_fill_(0, idx, False)
+        self._slot_cache.clear()
+        return slots
+
+    def evict_many(self, seq_ids: Sequence[Hashable]) -> None:
+        """NEW: :meth:`evict` of every id (host bookkeeping only)."""
+        for s in seq_ids:
+            self._free.append(self._slot_of.pop(s))
+        self._slot_cache.clear()
+
     # --- checkpoint / resume ------------------------------------------
     def state_dict(self) -> dict:
         """NEW: the config-set pool ([capacity, 266] int32), the broken flags
@@ -389,7 +411,7 @@ class CFGConstraintBatch:
         if hit is not None:
             self._slot_cache.move_to_end(key)
             return hit
-        slots = torch.tensor([self._slot_of[s] for s in key], dtype=torch.int64).to(self.device)
+        slots = _upload([self._slot_of[s] for s in key], torch.int64, self.device)
         self._slot_cache[key] = slots
         if len(self._slot_cache) > self._SLOT_CACHE:
             self._slot_cache.popitem(last=False)
@@ -442,6 +464,33 @@ class CFGConstraintBatch:
             self._configs.data_ptr(), slots.data_ptr(), self._broken.view(torch.uint8).data_ptr(),
             B, mbuf.data_ptr(), cap, ws.data_ptr(), float(neg_inf), tokens.data_ptr(),
             status.data_ptr(), int(chunks_per_row), _stream(logits)))
+        self.last_status = status
+        return tokens
+
+    def step_greedy_from(self, seq_ids: Sequence[Hashable], src: torch.Tensor,
+                         src_rows: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                         neg_inf: float = float("-inf"), chunks_per_row: int = 0,
+                         ) -> torch.Tensor:
+        """NEW: :meth:`step_greedy` on an fp32 working copy of the rows without
+        making the copy: row b reads ``src[src_rows[b]]`` (any float dtype;
+        rows 0..B-1 when ``src_rows`` is None), the masked fp32 row goes to
+        ``out[b]`` (None: nowhere), ``src`` is not modified."""
+        from ..ops import _ptr, _source_args
+
+        slots = self._slots(seq_ids)
+        B = int(slots.numel())
+        code, rows, out = _source_args(src, self.g.vocab_size, B, src_rows, out, self.device)
+        tokens = torch.empty(B, dtype=torch.int64, device=self.device)
+        status = torch.empty(B, dtype=torch.int32, device=self.device)
+        mbuf, cap = self.g.mask_memo()
+        ws = self.g.workspace(B)
+        L = _capi.lib()
+        L.check(L.bpd_pda_step_greedy_from(
+            C.byref(self.g._struct()), src.data_ptr(), code, src.stride(0), _ptr(rows), _ptr(out),
+            out.stride(0) if out is not None else 0, self._configs.data_ptr(), slots.data_ptr(),
+            self._broken.view(torch.uint8).data_ptr(), B, mbuf.data_ptr(), cap, ws.data_ptr(),
+            float(neg_inf), tokens.data_ptr(), status.data_ptr(), int(chunks_per_row),
+            _stream(src)))
         self.last_status = status
         return tokens
 

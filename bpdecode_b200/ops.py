@@ -26,6 +26,8 @@ from __future__ import annotations
 from dataclasses import dataclass, replace
 
 import numpy as np
+from collections.abc import Sequence
+
 import torch
 
 from . import _capi
@@ -68,6 +70,34 @@ def _check_logits(logits: torch.Tensor, vocab: int) -> int:
     return _DTYPE_CODE[logits.dtype]
 
 
+def _source_args(src: torch.Tensor, vocab: int, batch: int, src_rows: torch.Tensor | None,
+                 out: torch.Tensor | None, device: torch.device) -> tuple:
+    """(src code, row map, out) of the ``*_from`` steps: ``src`` [N, >= vocab]
+    any float dtype on the device (columns contiguous); ``src_rows`` int64
+    [batch] row indices into it, or None for rows 0..batch-1; ``out`` None or
+    fp32 [batch, >= vocab]."""
+    _require_cuda(src, "src")
+    if src.dim() != 2 or src.shape[1] < vocab or src.stride(1) != 1:
+        raise RuntimeError(f"bpdecode_b200: src must be [rows, >= {vocab}] with contiguous "
+                           f"columns, got {tuple(src.shape)} strides {src.stride()}")
+    if src.dtype not in _DTYPE_CODE:
+        raise RuntimeError(f"bpdecode_b200: unsupported src dtype {src.dtype}")
+    if src_rows is None:
+        if src.shape[0] < batch:
+            raise RuntimeError("bpdecode_b200: src has fewer rows than the batch")
+    else:
+        if (src_rows.dtype != torch.int64 or src_rows.numel() != batch
+                or src_rows.device != device):
+            raise RuntimeError("bpdecode_b200: src_rows must be int64 [batch] on the device")
+        src_rows = src_rows.contiguous()
+    if out is not None:
+        _require_cuda(out, "out")
+        if (out.dtype != torch.float32 or out.dim() != 2 or out.shape[0] != batch
+                or out.shape[1] < vocab or out.stride(1) != 1):
+            raise RuntimeError(f"bpdecode_b200: out must be fp32 [batch, >= {vocab}]")
+    return _DTYPE_CODE[src.dtype], src_rows, out
+
+
 def _as_i32(states: torch.Tensor, n: int, device: torch.device) -> torch.Tensor:
     _require_cuda(states, "states")
     if states.device != device:
@@ -78,6 +108,17 @@ def _as_i32(states: torch.Tensor, n: int, device: torch.device) -> torch.Tensor:
     if s.dtype != torch.int32:
         s = s.to(torch.int32)
     return s.contiguous()
+
+
+def _upload(values: Sequence[int], dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A small host list as a device tensor without a host synchronisation:
+    staged through page-locked memory (torch's caching host allocator) and
+    copied asynchronously on the current stream -- a copy from pageable
+    memory would wait for the work already queued on the GPU."""
+    host = torch.tensor(list(values), dtype=dtype)
+    if device.type != "cuda":
+        return host.to(device)
+    return host.pin_memory().to(device, non_blocking=True)
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:

@@ -129,7 +129,23 @@ bpd_status bpd_dense_step_greedy(
     int32_t num_states, float neg_inf, int64_t* token_out, int32_t* next_out,
     int32_t chunks_per_row, void* step_scratch, void* stream);
 
+/* NEW: the fused step on fp32 working values taken from another buffer --
+ * what a caller that upcasts 16-bit model logits to an fp32 copy before
+ * masking (hf.py:106-113) gets, without the copy. Row b reads row
+ * src_rows[b] of `src` (dtype BPD_F32 / BPD_BF16 / BPD_F16, row stride
+ * src_stride; src_rows may be NULL: row b), writes the masked fp32 row to
+ * out + b * out_stride (out may be NULL: nothing is written), then the argmax
+ * and commit as bpd_dense_step_greedy. `src` is never written. */
+bpd_status bpd_dense_step_greedy_from(
+    const void* src, int32_t src_dtype, int64_t src_stride, const int64_t* src_rows,
+    float* out, int64_t out_stride, int32_t batch, int32_t vocab_size,
+    int32_t* state_pool, const int64_t* slots, const uint32_t* allow_bits,
+    int32_t words_stride, const int32_t* tok_next, int32_t num_states,
+    float neg_inf, int64_t* token_out, int32_t* next_out, int32_t chunks_per_row,
+    void* step_scratch, void* stream);
+
 /* --------------------------------------------------------------------------
+ * Byte-walk path:/* --------------------------------------------------------------------------
  * Byte-walk path: the same ops on the raw symbol-class DFA, for automata
  * that are not densified (no tok_next table). trans int32 [num_states *
  * num_symbols], accept / live uint8 [num_states], tok_offsets int32 [vocab+1],
@@ -206,7 +222,19 @@ bpd_status bpd_soft_step_greedy(
     int64_t* token_out, int32_t* next_out, int32_t chunks_per_row,
     void* step_scratch, void* stream);
 
+/* NEW: bpd_soft_step_greedy on fp32 working values read from `src` (the
+ * source / destination contract of bpd_dense_step_greedy_from): the biased
+ * fp32 rows go to `out` (NULL: not written). */
+bpd_status bpd_soft_step_greedy_from(
+    const void* src, int32_t src_dtype, int64_t src_stride, const int64_t* src_rows,
+    float* out, int64_t out_stride, int32_t batch, int32_t vocab_size,
+    int32_t* state_pool, const int64_t* slots, const float* lookahead,
+    const uint32_t* allow_bits, int32_t words_stride, const int32_t* tok_next,
+    int32_t num_states, float alpha, int64_t* token_out, int32_t* next_out,
+    int32_t chunks_per_row, void* step_scratch, void* stream);
+
 /* --------------------------------------------------------------------------
+ * Pushdown automaton (context-free grammars)/* --------------------------------------------------------------------------
  * Pushdown automaton (context-free grammars)
  * ------------------------------------------------------------------------ */
 
@@ -279,7 +307,18 @@ bpd_status bpd_pda_step_greedy(
     void* memo, int32_t memo_capacity, void* workspace, float neg_inf,
     int64_t* token_out, int32_t* status_out, int32_t chunks_per_row, void* stream);
 
-/* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64).
+/* NEW: bpd_pda_step_greedy on fp32 working values read from `src` (the
+ * source / destination contract of bpd_dense_step_greedy_from); the reference
+ * PDA op takes fp32 logits only (torch_ops.cpp:334-335), which callers with
+ * 16-bit logits meet by upcasting a copy. */
+bpd_status bpd_pda_step_greedy_from(
+    const bpd_pda_grammar* g, const void* src, int32_t src_dtype,
+    int64_t src_stride, const int64_t* src_rows, float* out, int64_t out_stride,
+    int32_t* config_pool, const int64_t* slots, uint8_t* broken, int32_t batch,
+    void* memo, int32_t memo_capacity, void* workspace, float neg_inf,
+    int64_t* token_out, int32_t* status_out, int32_t chunks_per_row, void* stream);
+
+/* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64)./* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64).
  * ok_out[b] (uint8, may be NULL) = 1 if the token was accepted; a rejected
  * token leaves the config-set unchanged; EOS sets ok = complete and never
  * changes it (pda_cpu.cpp:35-54). If broken != NULL: broken[slot] |= !ok, and

@@ -251,6 +251,44 @@ def test_config2_fused_step_equals_unfused_and_oracle(orc: Oracle) -> None:
                               nxt.cpu().numpy()[rows])
 
 
+def test_config3_schema_steps_match_oracle(orc: Oracle) -> None:
+    """Config 3 (the JSON-Schema object as a dense DFA, V = 151,936, B = 512,
+    fp32 N(0, 1), greedy commit): every row of the first steps against the
+    oracle -- masked logits, tokens and states -- and the fused step against
+    the unfused one over 32 steps."""
+    from bpdecode_b200 import tables
+    from bpdecode_b200.batch import ConstraintBatch
+    from bpdecode_b200.ops import FsaTensors
+    from bpdecode_b200.workloads import vocab_large
+
+    B, V = 512, 151_936
+    fsa = FsaTensors.from_arrays(tables.load_dfa("schema"), vocab_large(V)).to("cuda")
+    a, b = ConstraintBatch(fsa, capacity=B), ConstraintBatch(fsa, capacity=B)
+    ids = list(range(B))
+    for i in ids:
+        a.add(i)
+        b.add(i)
+    tn = fsa.dense_tables()[0].cpu().numpy()
+    for step in range(32):
+        gen = torch.Generator(device="cuda").manual_seed(3000 + step)
+        logits = torch.randn(B, V, generator=gen, device="cuda")
+        before = a._state.cpu().numpy().copy()
+        la = logits.clone()
+        a.apply_mask(ids, la)
+        tok = la.argmax(-1)
+        nxt = a.commit(ids, tok)
+        lb = logits.clone()
+        assert torch.equal(b.step_greedy(ids, lb), tok)
+        assert torch.equal(lb, la) and torch.equal(a._state, b._state)
+        if step < 3:
+            want = logits.cpu().numpy()
+            orc.dense_apply_mask(want, tn, before, NINF)
+            assert np.array_equal(la.cpu().numpy(), want)
+            assert np.array_equal(np.argmax(want, axis=1), tok.cpu().numpy())
+            assert np.array_equal(orc.dense_advance(tn, before, tok.cpu().numpy()),
+                                  nxt.cpu().numpy())
+
+
 @pytest.mark.parametrize("k", [1, 2, 3, 7, 32])
 def test_step_chunkings_agree(k: int) -> None:
     """Any cut of the rows into work items gives the unfused result, and the
