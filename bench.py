@@ -167,6 +167,7 @@ def cpu_baseline(tok_next_cpu: torch.Tensor, starts: list[int], pats: list[int],
     """The reference's own dense torch step on host cores (all torch threads)."""
     from oracle import torch_port
 
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     state = torch.tensor([starts[p] for p in pats[:rows]], dtype=torch.int32)
     slots = torch.arange(rows)
     g = torch.Generator().manual_seed(12345)
@@ -193,6 +194,9 @@ def run_reference(args: argparse.Namespace) -> None:
     rank, world, _ = _dist()
     if rank != 0:
         return
+    # torchrun sets OMP_NUM_THREADS=1 per rank; rank 0 runs alone here, so it
+    # takes every host core it may use
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     from bpdecode_b200 import tables
     from bpdecode_b200.workloads import DENSE_PATTERNS, row_patterns, vocab_large
     from oracle.oracle import Oracle, dfa_with_vocab
