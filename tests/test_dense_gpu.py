@@ -466,3 +466,34 @@ def test_empty_batch_and_cpu_tensors_fail_loudly() -> None:
     with pytest.raises(RuntimeError):
         ops.apply_mask_(torch.zeros(1, fsa.vocab_size), fsa,
                         torch.zeros(1, dtype=torch.int32, device="cuda"))
+
+
+def test_invalid_tokens_and_states_are_rejected_not_read() -> None:
+    """Fault injection from the host: token ids outside [0, V) and states
+    outside [0, S) (the reference would read out of bounds) turn the row
+    BROKEN / fully masked instead; valid rows are unaffected."""
+    from bpdecode_b200.batch import BROKEN, ConstraintBatch
+
+    fsa = _ipv4_large(4096)
+    V, S = fsa.vocab_size, fsa.num_states
+    b = ConstraintBatch(fsa, capacity=8)
+    ids = list(range(8))
+    for i in ids:
+        b.add(i)
+    start = b.state_of(0)
+    digit = next(t for t in range(V) if int(fsa.dense_tables()[0][start, t]) >= 0)
+    toks = torch.tensor([-3, V, V + 100, digit, -1, digit, 2**40, digit], device="cuda")
+    nxt = b.commit(ids, toks)
+    bad = [0, 1, 2, 4, 6]
+    assert all(int(nxt[i]) == BROKEN for i in bad)
+    assert all(int(nxt[i]) >= 0 for i in (3, 5, 7))
+    # a state outside the table (corrupted pool entry) masks the whole row
+    b._state[b._slot_of[3]] = S + 7
+    logits = torch.randn(8, V, device="cuda")
+    b.apply_mask(ids, logits)
+    for i in bad + [3]:
+        assert torch.isneginf(logits[i]).all()
+    assert not torch.isneginf(logits[5]).all()
+    tok = b.step_greedy(ids, torch.randn(8, V, device="cuda"))
+    assert int(b.state_of(3)) == BROKEN and all(b.state_of(i) == BROKEN for i in bad)
+    assert torch.equal(tok[bad], torch.zeros(len(bad), dtype=torch.int64, device="cuda"))

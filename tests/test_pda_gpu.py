@@ -266,3 +266,27 @@ def test_fused_step_equals_unfused(name: str) -> None:
         assert torch.equal(b.last_status, st)
         assert torch.equal(a._configs, b._configs)
         assert torch.equal(a._broken, b._broken)
+
+
+def test_invalid_tokens_leave_config_unchanged_and_break_the_row() -> None:
+    """Fault injection from the host: a token id outside [0, V) is rejected
+    (ok = 0), the config-set is unchanged, the row is BROKEN (status -1) and
+    masked entirely afterwards; valid rows are unaffected."""
+    from bpdecode_b200.grammar.device import CFGConstraintBatch
+
+    g = _dev("jsonvalue_v4096")
+    b = CFGConstraintBatch(g, capacity=4)
+    for i in range(4):
+        b.add(i)
+    before = b._configs.clone()
+    V = g.vocab_size
+    logits = torch.randn(4, V, device="cuda")
+    b.apply_mask(list(range(4)), logits)
+    good = int(logits[3].argmax())
+    status = b.commit([0, 1, 2, 3], torch.tensor([-1, V, V + 9, good], device="cuda"))
+    assert status.tolist() == [-1, -1, -1, 1]
+    assert torch.equal(b._configs[:3], before[:3])
+    assert b._broken[:3].all() and not bool(b._broken[3])
+    masked = torch.randn(4, V, device="cuda")
+    b.apply_mask(list(range(4)), masked)
+    assert torch.isneginf(masked[:3]).all() and not torch.isneginf(masked[3]).all()

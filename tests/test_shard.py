@@ -54,3 +54,38 @@ def test_single_process_is_identity() -> None:
     assert shard.shard_rows(7, 3, 2) == range(5, 7)
     assert shard.max_over_ranks([1.0, 2.0]) == [1.0, 2.0]
     assert torch.distributed.is_available()
+
+
+def _lost_rank_worker(rank: int, world: int, port: int, out) -> None:
+    """Rank 1 leaves between steps (before the barrier that closes the timed
+    region); rank 0 must get an error from its next collective, not hang."""
+    import time
+
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from bpdecode_b200 import shard
+
+    assert shard.init("gloo", timeout_s=5)
+    shard.barrier()  # both ranks are up
+    if rank == 1:
+        os._exit(0)  # leaves without the group's next collective
+    t0 = time.monotonic()
+    try:
+        shard.max_over_ranks([1.0])
+        out.put((rank, "no error", time.monotonic() - t0))
+    except Exception as exc:  # noqa: BLE001 -- any collective error is the signal
+        out.put((rank, type(exc).__name__, time.monotonic() - t0))
+    os._exit(0)
+
+
+def test_lost_rank_ends_the_others_collective_with_an_error() -> None:
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    ctx_procs = mp.start_processes(_lost_rank_worker, args=(world, _free_port(), q),
+                                   nprocs=world, join=False, start_method="spawn")
+    rank, err, waited = q.get()
+    for p in ctx_procs.processes:
+        p.join(timeout=60)
+    assert rank == 0 and err != "no error"
+    assert waited < 30  # the short process-group timeout, not a hang
