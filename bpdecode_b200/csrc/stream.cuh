@@ -572,10 +572,11 @@ __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
                        Rows rows, Commit commit, typename Dt<T>::Bits fill, int32_t chunk,
                        int32_t chunks_per_row, StepScratch ws) {
   extern __shared__ __align__(16) uint8_t smem[];
-  if constexpr (kVec) {
-    fill_init<T>(smem, fill);
-    __syncthreads();
-  }
+  __shared__ unsigned long long warp_q[kWarps];
+  __shared__ uint32_t warps_done;
+  if (threadIdx.x == 0) warps_done = 0u;
+  if constexpr (kVec) fill_init<T>(smem, fill);
+  __syncthreads();
   const int32_t row = blockIdx.x / chunks_per_row;
   const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
   const WarpShare sh = warp_share<T, kVec>(c0, min(V, c0 + chunk));
@@ -593,18 +594,35 @@ __global__ void __launch_bounds__(kThreads, BPD_STEP_MIN_BLOCKS)
                                                      sh.s1, info.brow, fill,
                                                      reinterpret_cast<const uint4*>(smem),
                                                      info.lrow, rows_alpha(rows), st, issued);
+  // Two-level last-arriver merge, no barrier: the CTA's last warp (a shared
+  // memory count) merges the CTA's 8 partials and takes part in the row's
+  // count in global memory; the row's last CTA commits.
   const unsigned long long q = warp_max_u64(pack_arg(st.key, st.idx));
   const int32_t lane = threadIdx.x & 31;
   int32_t tok = -1;
   if (lane == 0) {
-    atomicMax(ws.best + row, q);
-    __threadfence();
-    const uint32_t parts = static_cast<uint32_t>(chunks_per_row * kWarps);
-    if (atomicAdd(ws.done + row, 1u) == parts - 1u) {
-      __threadfence();
-      const unsigned long long b = atomicExch(ws.best + row, 0ull);
-      ws.done[row] = 0u;
-      tok = unpack_idx(b);
+    warp_q[threadIdx.x >> 5] = q;
+    __threadfence_block();
+    if (atomicAdd(&warps_done, 1u) == kWarps - 1) {
+      __threadfence_block();
+      unsigned long long m = 0;
+#pragma unroll
+      for (int i = 0; i < kWarps; ++i) {
+        const unsigned long long x = *static_cast<volatile unsigned long long*>(&warp_q[i]);
+        m = x > m ? x : m;
+      }
+      if (chunks_per_row == 1) {
+        tok = unpack_idx(m);
+      } else {
+        atomicMax(ws.best + row, m);
+        __threadfence();
+        if (atomicAdd(ws.done + row, 1u) == static_cast<uint32_t>(chunks_per_row - 1)) {
+          __threadfence();
+          const unsigned long long b = atomicExch(ws.best + row, 0ull);
+          ws.done[row] = 0u;
+          tok = unpack_idx(b);
+        }
+      }
     }
     if (issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
