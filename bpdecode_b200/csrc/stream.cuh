@@ -469,10 +469,22 @@ struct DenseCommit {
 // Chunk of one CTA: `chunks_per_row` CTAs per row when the caller asks for
 // it, else BPD_TILES_PER_WARP warp tiles per warp. Always a multiple of
 // kWarps warp tiles, so every warp span starts on a tile.
+//
+// With `batch` given, small batches are cut finer (down to one warp tile per
+// warp) until the grid has about one CTA per SM, so a step over a handful of
+// rows is not a few CTAs working through their tiles one after another
+// (B = 1, V = 128,256: 13.9 -> 11.9 us per step replayed from a graph).
 template <typename T>
-inline int32_t stream_chunk(int32_t V, int32_t chunks_per_row) {
+inline int32_t stream_chunk(int32_t V, int32_t chunks_per_row, int32_t batch = 0) {
   constexpr int32_t UNIT = tile_elems<T>() * kWarps;
-  if (chunks_per_row <= 0) return UNIT * BPD_TILES_PER_WARP;
+  if (chunks_per_row <= 0) {
+    int32_t tpw = BPD_TILES_PER_WARP;
+    const int64_t want = static_cast<int64_t>(sm_count());
+    while (tpw > 1 && batch > 0 &&
+           static_cast<int64_t>(batch) * ((V + UNIT * tpw - 1) / (UNIT * tpw)) < want)
+      tpw /= 2;
+    return UNIT * tpw;
+  }
   const int32_t per = (V + chunks_per_row - 1) / chunks_per_row;
   return ((per + UNIT - 1) / UNIT) * UNIT;
 }
@@ -644,7 +656,7 @@ template <typename T, class Rows>
 bpd_status launch_stream_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
                                const Rows& rows, float neg_inf, cudaStream_t st,
                                const char* what) {
-  const int32_t chunk = stream_chunk<T>(V, 0);
+  const int32_t chunk = stream_chunk<T>(V, 0, batch);
   const int32_t chunks = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * chunks;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
@@ -668,7 +680,7 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
   if (!aligned16(scratch))
     return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
-  const int32_t chunk = stream_chunk<T>(V, chunks_per_row);
+  const int32_t chunk = stream_chunk<T>(V, chunks_per_row, batch);
   const int32_t cpr = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * cpr;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
@@ -702,7 +714,7 @@ bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int
   if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
   if (!aligned16(scratch))
     return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
-  const int32_t chunk = stream_chunk<float>(V, chunks_per_row);
+  const int32_t chunk = stream_chunk<float>(V, chunks_per_row, batch);
   const int32_t cpr = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * cpr;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
