@@ -87,6 +87,22 @@ struct Dt<__half> {
   __device__ static Bits from_float_dev(float f) { return __half_as_ushort(__float2half_rn(f)); }
 };
 
+// Calls f(T{}) with T the logits element type of `dtype` (BPD_F32 / BPD_BF16 /
+// BPD_F16), or fails with "<what>: unsupported <kind> dtype".
+template <class F>
+bpd_status with_dtype(int32_t dtype, const char* what, F&& f, const char* kind = "logits") {
+  switch (dtype) {
+    case BPD_F32:
+      return f(float{});
+    case BPD_BF16:
+      return f(__nv_bfloat16{});
+    case BPD_F16:
+      return f(__half{});
+    default:
+      return fail(BPD_ERR_INVALID, "%s: unsupported %s dtype %d", what, kind, dtype);
+  }
+}
+
 constexpr size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
 __device__ __forceinline__ uint32_t vec_word(const uint4& v, int i) {

@@ -116,7 +116,6 @@ __global__ void dense_mask_bits_kernel(const int32_t* __restrict__ pool,
 
 int esize(int32_t dtype) { return dtype == BPD_F32 ? 4 : 2; }
 
-bool dtype_ok(int32_t dtype) { return dtype == BPD_F32 || dtype == BPD_BF16 || dtype == BPD_F16; }
 
 template <typename T>
 bpd_status launch_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
@@ -184,22 +183,15 @@ extern "C" bpd_status bpd_dense_apply_mask(void* logits, int32_t dtype, int64_t 
   BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_dense_apply_mask: bad sizes");
   if (batch == 0) return BPD_OK;
   BPD_REQUIRE(logits && state_pool && allow_bits, "bpd_dense_apply_mask: null pointer");
-  BPD_REQUIRE(dtype_ok(dtype), "bpd_dense_apply_mask: unsupported logits dtype %d", dtype);
   BPD_REQUIRE(row_stride >= vocab_size, "bpd_dense_apply_mask: row_stride < vocab");
   BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32, "bpd_dense_apply_mask: words_stride too small");
   (void)esize;
   cudaStream_t st = as_stream(stream);
-  switch (dtype) {
-    case BPD_F32:
-      return launch_apply<float>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                 allow_bits, words_stride, num_states, neg_inf, st);
-    case BPD_BF16:
-      return launch_apply<__nv_bfloat16>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                         allow_bits, words_stride, num_states, neg_inf, st);
-    default:
-      return launch_apply<__half>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                  allow_bits, words_stride, num_states, neg_inf, st);
-  }
+  return with_dtype(dtype, "bpd_dense_apply_mask", [&](auto tag) {
+    using T = decltype(tag);
+    return launch_apply<T>(logits, row_stride, batch, vocab_size, state_pool, slots, allow_bits,
+                           words_stride, num_states, neg_inf, st);
+  });
 }
 
 extern "C" bpd_status bpd_dense_advance(int32_t* state_pool, const int64_t* slots, int32_t batch,
@@ -247,27 +239,18 @@ extern "C" bpd_status bpd_dense_step_greedy(void* logits, int32_t dtype, int64_t
   if (batch == 0) return BPD_OK;
   BPD_REQUIRE(logits && state_pool && allow_bits && tok_next && token_out,
               "bpd_dense_step_greedy: null pointer");
-  BPD_REQUIRE(dtype_ok(dtype), "bpd_dense_step_greedy: unsupported logits dtype %d", dtype);
   BPD_REQUIRE(row_stride >= vocab_size, "bpd_dense_step_greedy: row_stride < vocab");
   BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
               "bpd_dense_step_greedy: words_stride too small");
   BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
               "bpd_dense_step_greedy: chunks_per_row must be in [0, 4096]");
   cudaStream_t st = as_stream(stream);
-  switch (dtype) {
-    case BPD_F32:
-      return launch_step<float>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                allow_bits, words_stride, tok_next, num_states, neg_inf,
-                                token_out, next_out, chunks_per_row, step_scratch, st);
-    case BPD_BF16:
-      return launch_step<__nv_bfloat16>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                        allow_bits, words_stride, tok_next, num_states, neg_inf,
-                                        token_out, next_out, chunks_per_row, step_scratch, st);
-    default:
-      return launch_step<__half>(logits, row_stride, batch, vocab_size, state_pool, slots,
-                                 allow_bits, words_stride, tok_next, num_states, neg_inf,
-                                 token_out, next_out, chunks_per_row, step_scratch, st);
-  }
+  return with_dtype(dtype, "bpd_dense_step_greedy", [&](auto tag) {
+    using T = decltype(tag);
+    return launch_step<T>(logits, row_stride, batch, vocab_size, state_pool, slots, allow_bits,
+                          words_stride, tok_next, num_states, neg_inf, token_out, next_out,
+                          chunks_per_row, step_scratch, st);
+  });
 }
 
 extern "C" bpd_status bpd_dense_step_greedy_from(
@@ -290,21 +273,10 @@ extern "C" bpd_status bpd_dense_step_greedy_from(
   const DenseRows rows{state_pool, slots, allow_bits, words_stride, num_states};
   const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
   const char* what = "bpd_dense_step_greedy_from";
-  switch (src_dtype) {
-    case BPD_F32:
-      return launch_stream_step_src<float, DenseRows, DenseCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, neg_inf,
-          chunks_per_row, step_scratch, st, what);
-    case BPD_BF16:
-      return launch_stream_step_src<__nv_bfloat16, DenseRows, DenseCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, neg_inf,
-          chunks_per_row, step_scratch, st, what);
-    case BPD_F16:
-      return launch_stream_step_src<__half, DenseRows, DenseCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, neg_inf,
-          chunks_per_row, step_scratch, st, what);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_dense_step_greedy_from: unsupported source dtype %d",
-                  src_dtype);
-  }
+  return with_dtype(src_dtype, what, [&](auto tag) {
+    using T = decltype(tag);
+    return launch_stream_step_src<T, DenseRows, DenseCommit>(
+        src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, neg_inf,
+        chunks_per_row, step_scratch, st, what);
+  }, "source");
 }

@@ -845,18 +845,10 @@ extern "C" bpd_status bpd_pda_apply_mask(const bpd_pda_grammar* g, void* logits,
   bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
                                     workspace, &m, &w, st);
   if (rc) return rc;
-  switch (dtype) {
-    case BPD_F32:
-      return launch_pda_apply<float>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf, st);
-    case BPD_BF16:
-      return launch_pda_apply<__nv_bfloat16>(logits, row_stride, batch, g->vocab_size, m, w,
-                                             neg_inf, st);
-    case BPD_F16:
-      return launch_pda_apply<__half>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
-                                      st);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_pda_apply_mask: unsupported logits dtype %d", dtype);
-  }
+  return with_dtype(dtype, "bpd_pda_apply_mask", [&](auto tag) {
+    using T = decltype(tag);
+    return launch_pda_apply<T>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf, st);
+  });
 }
 
 extern "C" bpd_status bpd_pda_step_greedy(
@@ -878,19 +870,11 @@ extern "C" bpd_status bpd_pda_step_greedy(
   if (rc) return rc;
   const int32_t k = chunks_per_row;
   const PdaCommit commit{*g, config_pool, slots, token_out, broken, status_out};
-  switch (dtype) {
-    case BPD_F32:
-      return launch_pda_step<float>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
-                                    commit, k, st);
-    case BPD_BF16:
-      return launch_pda_step<__nv_bfloat16>(logits, row_stride, batch, g->vocab_size, m, w,
-                                            neg_inf, commit, k, st);
-    case BPD_F16:
-      return launch_pda_step<__half>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf,
-                                     commit, k, st);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_pda_step_greedy: unsupported logits dtype %d", dtype);
-  }
+  return with_dtype(dtype, "bpd_pda_step_greedy", [&](auto tag) {
+    using T = decltype(tag);
+    return launch_pda_step<T>(logits, row_stride, batch, g->vocab_size, m, w, neg_inf, commit,
+                              k, st);
+  });
 }
 
 extern "C" bpd_status bpd_pda_step_greedy_from(
@@ -917,23 +901,12 @@ extern "C" bpd_status bpd_pda_step_greedy_from(
   const PdaRows rows{m, w};
   const int32_t V = g->vocab_size;
   const char* what = "bpd_pda_step_greedy_from";
-  switch (src_dtype) {
-    case BPD_F32:
-      return launch_stream_step_src<float, PdaRows, PdaCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
-          chunks_per_row, w.step, st, what);
-    case BPD_BF16:
-      return launch_stream_step_src<__nv_bfloat16, PdaRows, PdaCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
-          chunks_per_row, w.step, st, what);
-    case BPD_F16:
-      return launch_stream_step_src<__half, PdaRows, PdaCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
-          chunks_per_row, w.step, st, what);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_pda_step_greedy_from: unsupported source dtype %d",
-                  src_dtype);
-  }
+  return with_dtype(src_dtype, what, [&](auto tag) {
+    using T = decltype(tag);
+    return launch_stream_step_src<T, PdaRows, PdaCommit>(
+        src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
+        chunks_per_row, w.step, st, what);
+  }, "source");
 }
 
 extern "C" bpd_status bpd_pda_advance(const bpd_pda_grammar* g, int32_t* config_pool,

@@ -192,16 +192,10 @@ extern "C" bpd_status bpd_soft_apply(void* logits, int32_t dtype, int64_t row_st
   cudaStream_t st = as_stream(stream);
   const SoftRows rows{const_cast<int32_t*>(state_pool), slots, allow_bits, words_stride,
                       lookahead, num_states, vocab_size, alpha};
-  switch (dtype) {
-    case BPD_F32:
-      return launch_soft_apply<float>(logits, row_stride, batch, vocab_size, rows, st);
-    case BPD_BF16:
-      return launch_soft_apply<__nv_bfloat16>(logits, row_stride, batch, vocab_size, rows, st);
-    case BPD_F16:
-      return launch_soft_apply<__half>(logits, row_stride, batch, vocab_size, rows, st);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_soft_apply: unsupported logits dtype %d", dtype);
-  }
+  return with_dtype(dtype, "bpd_soft_apply", [&](auto tag) {
+    using T = decltype(tag);
+    return launch_soft_apply<T>(logits, row_stride, batch, vocab_size, rows, st);
+  });
 }
 
 extern "C" bpd_status bpd_soft_step_greedy(void* logits, int32_t dtype, int64_t row_stride,
@@ -225,19 +219,11 @@ extern "C" bpd_status bpd_soft_step_greedy(void* logits, int32_t dtype, int64_t 
   const SoftRows rows{state_pool, slots, allow_bits, words_stride, lookahead, num_states,
                       vocab_size, alpha};
   const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
-  switch (dtype) {
-    case BPD_F32:
-      return launch_soft_step<float>(logits, row_stride, batch, vocab_size, rows, commit,
-                                     chunks_per_row, step_scratch, st);
-    case BPD_BF16:
-      return launch_soft_step<__nv_bfloat16>(logits, row_stride, batch, vocab_size, rows, commit,
-                                             chunks_per_row, step_scratch, st);
-    case BPD_F16:
-      return launch_soft_step<__half>(logits, row_stride, batch, vocab_size, rows, commit,
-                                      chunks_per_row, step_scratch, st);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_soft_step_greedy: unsupported logits dtype %d", dtype);
-  }
+  return with_dtype(dtype, "bpd_soft_step_greedy", [&](auto tag) {
+    using T = decltype(tag);
+    return launch_soft_step<T>(logits, row_stride, batch, vocab_size, rows, commit,
+                               chunks_per_row, step_scratch, st);
+  });
 }
 
 extern "C" bpd_status bpd_soft_step_greedy_from(
@@ -262,21 +248,10 @@ extern "C" bpd_status bpd_soft_step_greedy_from(
                       vocab_size, alpha};
   const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
   const char* what = "bpd_soft_step_greedy_from";
-  switch (src_dtype) {
-    case BPD_F32:
-      return launch_stream_step_src<float, SoftRows, DenseCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
-          chunks_per_row, step_scratch, st, what);
-    case BPD_BF16:
-      return launch_stream_step_src<__nv_bfloat16, SoftRows, DenseCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
-          chunks_per_row, step_scratch, st, what);
-    case BPD_F16:
-      return launch_stream_step_src<__half, SoftRows, DenseCommit>(
-          src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
-          chunks_per_row, step_scratch, st, what);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_soft_step_greedy_from: unsupported source dtype %d",
-                  src_dtype);
-  }
+  return with_dtype(src_dtype, what, [&](auto tag) {
+    using T = decltype(tag);
+    return launch_stream_step_src<T, SoftRows, DenseCommit>(
+        src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
+        chunks_per_row, step_scratch, st, what);
+  }, "source");
 }

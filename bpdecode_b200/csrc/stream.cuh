@@ -490,8 +490,9 @@ inline int32_t stream_chunk(int32_t V, int32_t chunks_per_row, int32_t batch = 0
 }
 
 // This warp's share of the CTA chunk [c0, c1): with the vector path, the
-// chunk's full tiles w, w + kWarps, ... (adjacent warps on adjacent tiles) and,
-// for the last warp, the ragged end; without it a contiguous element range.
+// chunk's full 16-bit tiles w, w + kWarps, ... (adjacent warps on adjacent
+// tiles) or a contiguous run of fp32 tiles, and for the last warp the ragged
+// end; without the vector path a contiguous element range.
 struct WarpShare {
   int32_t e0, nt, tstep, s0, s1;
 };
@@ -503,9 +504,18 @@ __device__ __forceinline__ WarpShare warp_share(int32_t c0, int32_t c1) {
   WarpShare r;
   if constexpr (kVec) {
     const int32_t ntc = c1 > c0 ? (c1 - c0) / TILE : 0;
-    r.e0 = c0 + w * TILE;
-    r.nt = ntc > w ? (ntc - w + kWarps - 1) / kWarps : 0;
-    r.tstep = kWarps * TILE;
+    if constexpr (sizeof(typename Dt<T>::Bits) == 4) {
+      // fp32 tiles (512 elements): a contiguous run of tiles per warp, so
+      // rejected runs go out in fewer, larger bulk stores (soft step -4 %)
+      const int32_t per = (ntc + kWarps - 1) / kWarps;
+      r.e0 = c0 + w * per * TILE;
+      r.nt = max(0, min(per, ntc - w * per));
+      r.tstep = TILE;
+    } else {
+      r.e0 = c0 + w * TILE;
+      r.nt = ntc > w ? (ntc - w + kWarps - 1) / kWarps : 0;
+      r.tstep = kWarps * TILE;
+    }
     r.s0 = c0 + ntc * TILE;
     r.s1 = w == kWarps - 1 ? max(r.s0, c1) : r.s0;
   } else {

@@ -129,17 +129,10 @@ extern "C" bpd_status bpd_walk_apply_mask(void* logits, int32_t dtype, int64_t r
   BPD_REQUIRE(logits && states, "bpd_walk_apply_mask: null pointer");
   BPD_REQUIRE(row_stride >= vocab_size, "bpd_walk_apply_mask: row_stride < vocab");
   cudaStream_t st = as_stream(stream);
-  switch (dtype) {
-    case BPD_F32:
-      return launch_walk_mask<float>(d, states, batch, logits, row_stride, neg_inf, nullptr, st);
-    case BPD_BF16:
-      return launch_walk_mask<__nv_bfloat16>(d, states, batch, logits, row_stride, neg_inf,
-                                             nullptr, st);
-    case BPD_F16:
-      return launch_walk_mask<__half>(d, states, batch, logits, row_stride, neg_inf, nullptr, st);
-    default:
-      return fail(BPD_ERR_INVALID, "bpd_walk_apply_mask: unsupported logits dtype %d", dtype);
-  }
+  return with_dtype(dtype, "bpd_walk_apply_mask", [&](auto tag) {
+    using T = decltype(tag);
+    return launch_walk_mask<T>(d, states, batch, logits, row_stride, neg_inf, nullptr, st);
+  });
 }
 
 extern "C" bpd_status bpd_walk_mask_bits(const int32_t* trans, int32_t num_states,
