@@ -472,6 +472,7 @@ def main() -> None:
     barrier()
     elapsed_ms = t_all0.elapsed_time(t_all1)
     kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
+    rank_ms = shard.gather_over_ranks(elapsed_ms, device)
     elapsed_ms, kern_ms = shard.max_over_ranks([elapsed_ms, kern_ms], device)
 
     total_rows = ROWS_PER_GPU * world * args.steps
@@ -527,6 +528,7 @@ def main() -> None:
                      "kernel_ms": kern_ms,
                      "algo_bytes_per_row_step": ALGO_BYTES_PER_ROW_STEP},
         "clocks": clocks.summary(),
+        "rank_ms": rank_ms,
         "gpu_launches": args.steps,
         "e2e": e2e,
         "unfused_dropin": {"ms_per_step": un_ms, "value": ROWS_PER_GPU * world / (un_ms / 1e3),

@@ -66,6 +66,18 @@ def sum_over_ranks(values: list[float], device: torch.device | None = None) -> l
     return _reduce(values, "sum", device)
 
 
+def gather_over_ranks(value: float, device: torch.device | None = None) -> list[float]:
+    """``value`` of every rank, in rank order (``[value]`` without a group)."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [float(value)]
+    t = torch.zeros(dist.get_world_size(), dtype=torch.float64, device=device)
+    t[dist.get_rank()] = value
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return [float(x) for x in t.tolist()]
+
+
 def barrier() -> None:
     import torch.distributed as dist
 

@@ -28,8 +28,9 @@ def _worker(rank: int, world: int, port: int, out) -> None:
     elapsed = [1.5 + rank, 10.0 * rank]
     mx = shard.max_over_ranks(elapsed)
     tot = shard.sum_over_ranks([float(len(rows))])
+    per = shard.gather_over_ranks(3.0 + rank)
     shard.barrier()
-    out.put((rank, list(rows), len(pats), mx, tot))
+    out.put((rank, list(rows), len(pats), mx, tot, per))
     shard.finish()
 
 
@@ -41,10 +42,11 @@ def test_two_ranks_shard_rows_and_reduce_timings() -> None:
                        start_method="spawn")
     got = sorted(q.get() for _ in range(world))
     assert got[0][1] == [0, 1, 2, 3, 4] and got[1][1] == [5, 6, 7, 8, 9]
-    for _, _, n, mx, tot in got:
+    for _, _, n, mx, tot, per in got:
         assert n == 5
         assert mx == [2.5, 10.0]  # max over ranks of every entry
         assert tot == [10.0]
+        assert per == [3.0, 4.0]  # every rank's value, in rank order
 
 
 def test_single_process_is_identity() -> None:
