@@ -52,10 +52,12 @@ typedef int32_t bpd_status;
 #define BPD_PDA_MAX_DEPTH 32
 #define BPD_PDA_CONFIG_INTS (2 + BPD_PDA_MAX_CONFIGS + BPD_PDA_MAX_CONFIGS * BPD_PDA_MAX_DEPTH)
 
-/* Library version string. */
+/* NEW (no reference counterpart; the reference reports errors through
+ * TORCH_CHECK exceptions, bindings/torch_ops.cpp:47-51): library version. */
 const char* bpd_version(void);
 
-/* Message of the last failed call on this host thread ("" if none). */
+/* NEW: message of the last failed call on this host thread ("" if none) --
+ * what the reference's TORCH_CHECK message carries. */
 const char* bpd_last_error(void);
 
 /* --------------------------------------------------------------------------
@@ -271,7 +273,9 @@ size_t bpd_pda_memo_bytes(int32_t capacity, int32_t vocab_size);
 bpd_status bpd_pda_memo_reset(void* memo, int32_t capacity, int32_t vocab_size,
                               void* stream);
 
-/* Per-call scratch of bpd_pda_apply_mask / bpd_pda_mask_bits for `batch` rows. */
+/* NEW: per-call scratch of bpd_pda_apply_mask / bpd_pda_mask_bits /
+ * bpd_pda_step_greedy for `batch` rows (the reference allocates its per-row
+ * PdaConfigSet copies in local memory inside its kernels, pda_cuda.cu:40-95). */
 size_t bpd_pda_workspace_bytes(int32_t batch, int32_t vocab_size);
 
 /* Packed allow bits per row, int32 [batch, ceil(vocab/32)], of config-set
