@@ -251,7 +251,7 @@ def _config(world: int) -> dict:
     return {
         "workload": "dense regex step at serving scale: 8 regexes mixed per batch, "
                     f"V={V}, {ROWS_PER_GPU} rows per GPU, bf16 logits N(0,{SIGMA:g}), argmax "
-                    f"commit, {EPISODE}-step generations (BASELINE config 2)",
+                    f"commit, {EPISODE}-step generations (config 2)",
         "vocab": V, "rows_per_gpu": ROWS_PER_GPU, "global_batch": ROWS_PER_GPU * world,
         "parallelism": f"dp{world} (rows sharded by request, no collective)",
         "l2": "inputs larger than L2: every step reads a 262 MB logits buffer (126 MB L2)",
