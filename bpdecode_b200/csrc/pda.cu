@@ -455,6 +455,7 @@ __device__ __forceinline__ void first_byte_items(const bpd_pda_grammar& g,
                                                  const Work& w, int32_t* scratch) {
   const int lane = threadIdx.x & 31;
   const int32_t items = w.counters[0] * 256;
+  if (items == 0) return;  // every row hit the memo: no item, no atomics
   for (;;) {
     int32_t item = 0;
     if (lane == 0) item = atomicAdd(w.counters + 2, 1);
@@ -490,6 +491,7 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
   const int32_t V = g.vocab_size;
   const int32_t chunks = (V + kComputeChunk - 1) / kComputeChunk;
   const int32_t items = w.counters[0] * chunks;
+  if (items == 0) return;  // the same value for every thread of the CTA
   for (;;) {
     __syncthreads();  // the previous item's shared state is no longer read
     if (threadIdx.x == 0) s_item = atomicAdd(w.counters + 1, 1);

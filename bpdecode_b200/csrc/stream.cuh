@@ -279,7 +279,17 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
       for (int t = 0; t < kGroupTiles; ++t)
         live |= (__any_sync(kAll, w[t] != 0u) ? 1u : 0u) << t;
       const int32_t ng = min(kGroupTiles, ntiles - g0);
-      const uint32_t dead = ((1u << ng) - 1u) & ~live;
+      uint32_t dead = ((1u << ng) - 1u) & ~live;
+      if constexpr (sizeof(Bits) == 4) {
+        // fp32: only a whole dead group goes out as one bulk store; dead
+        // tiles among live ones take plain stores with them (-4 % on the
+        // PDA step, neutral on the soft step; 16-bit rows keep every dead
+        // tile on the bulk engine, which is faster there)
+        if (dead != (1u << ng) - 1u) {
+          live |= dead;
+          dead = 0u;
+        }
+      }
       if (dead != 0u && lane == 0) {
         fill_first = min(fill_first, e0 + (g0 + __ffs(dead) - 1) * TILE);
         uint32_t d = row != nullptr ? dead : 0u;
