@@ -226,6 +226,25 @@ class ConstraintBatch:
         """NEW: :meth:`add` of every id (grammar index per id, or one for
         all) with one device write for the whole group."""
         gs = [grammars] * len(seq_ids) if isinstance(grammars, int) else list(grammars)
+        slots, starts = self._add_host(seq_ids, gs)
+        if slots:
+            idx = _upload(slots, torch.int64, self.device)
+            val = _upload(starts, torch.int32, self.device)
+            self._state.index_copy_(0, idx, val)
+        return slots
+
+    def evict_many(self, seq_ids: Sequence[Hashable]) -> None:
+        """NEW: :meth:`evict` of every id with one device write."""
+        slots = self._evict_host(seq_ids)
+        if slots:
+            idx = _upload(slots, torch.int64, self.device)
+            self._state.index_fill_(0, idx, FREE)
+
+    def _add_host(self, seq_ids: Sequence[Hashable], gs: Sequence[int],
+                  ) -> tuple[list[int], list[int]]:
+        """The bookkeeping of :meth:`add_many` (slots taken, grammars recorded)
+        without the device write: returns the slots and the start state each
+        must be given."""
         if len(gs) != len(seq_ids) or len(set(seq_ids)) != len(seq_ids):
             raise ValueError("add_many: one grammar per id, ids distinct")
         if any(s in self._slot_of for s in seq_ids):
@@ -236,23 +255,18 @@ class ConstraintBatch:
         for sid, slot, g in zip(seq_ids, slots, gs):
             self._slot_of[sid] = slot
             self._grammar_of[sid] = g
-        if slots:
-            idx = _upload(slots, torch.int64, self.device)
-            val = _upload([self._t.starts[g] for g in gs], torch.int32, self.device)
-            self._state.index_copy_(0, idx, val)
         self._slot_cache.clear()
-        return slots
+        return slots, [self._t.starts[g] for g in gs]
 
-    def evict_many(self, seq_ids: Sequence[Hashable]) -> None:
-        """NEW: :meth:`evict` of every id with one device write."""
+    def _evict_host(self, seq_ids: Sequence[Hashable]) -> list[int]:
+        """The bookkeeping of :meth:`evict_many` without the device write:
+        returns the freed slots (their state must become FREE)."""
         slots = [self._slot_of.pop(s) for s in seq_ids]
         for s in seq_ids:
             self._grammar_of.pop(s, None)
-        if slots:
-            idx = _upload(slots, torch.int64, self.device)
-            self._state.index_fill_(0, idx, FREE)
         self._free.extend(slots)
         self._slot_cache.clear()
+        return slots
 
     def reset_many(self, seq_ids: Sequence[Hashable]) -> None:
         """NEW: :meth:`reset` of every id in ``seq_ids`` as one device write on
@@ -467,10 +481,16 @@ class ConstraintBatch:
     ) -> torch.Tensor:
         """NEW: :meth:`soft_step_greedy` on an fp32 working copy of the rows
         without making the copy (the contract of :meth:`step_greedy_from`)."""
+        return self._soft_step_from_slots(self._slots(seq_ids), src, src_rows, out, alpha,
+                                          chunks_per_row)
+
+    def _soft_step_from_slots(self, slots: torch.Tensor, src: torch.Tensor,
+                              src_rows: torch.Tensor | None, out: torch.Tensor | None,
+                              alpha: float, chunks_per_row: int = 0) -> torch.Tensor:
+        """:meth:`soft_step_greedy_from` on device slot indices (int64)."""
         t = self._t
         if t.lookahead is None:
             raise ValueError("fsa has no lookahead table; build with dense + with_lookahead")
-        slots = self._slots(seq_ids)
         B = int(slots.numel())
         code, rows, out = _source_args(src, t.vocab_size, B, src_rows, out, self.device)
         tokens = torch.empty(B, dtype=torch.int64, device=self.device)

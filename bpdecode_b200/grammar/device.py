@@ -356,6 +356,14 @@ class CFGConstraintBatch:
 
     def add_many(self, seq_ids: Sequence[Hashable]) -> list[int]:
         """NEW: :meth:`add` of every id with one device write per pool."""
+        slots = self._add_host(seq_ids)
+        if slots:
+            self._init_slots(_upload(slots, torch.int64, self.device))
+        return slots
+
+    def _add_host(self, seq_ids: Sequence[Hashable]) -> list[int]:
+        """The bookkeeping of :meth:`add_many` without the device write (the
+        slots returned must get :meth:`_init_slots`)."""
         if len(set(seq_ids)) != len(seq_ids) or any(s in self._slot_of for s in seq_ids):
             raise KeyError("add_many: ids must be distinct and new")
         if len(seq_ids) > len(self._free):
@@ -363,12 +371,14 @@ class CFGConstraintBatch:
         slots = [self._free.pop() for _ in seq_ids]
         for sid, slot in zip(seq_ids, slots):
             self._slot_of[sid] = slot
-        if slots:
-            idx = _upload(slots, torch.int64, self.device)
-            self._configs.index_copy_(0, idx, self.g.init_batch(len(slots)))
-            self._broken.index_fill_(0, idx, False)
         self._slot_cache.clear()
         return slots
+
+    def _init_slots(self, idx: torch.Tensor) -> None:
+        """Fresh initial config-sets and cleared broken flags at device slot
+        indices ``idx`` (int64)."""
+        self._configs.index_copy_(0, idx, self.g.init_batch(int(idx.numel())))
+        self._broken.index_fill_(0, idx, False)
 
     def evict_many(self, seq_ids: Sequence[Hashable]) -> None:
         """NEW: :meth:`evict` of every id (host bookkeeping only)."""
@@ -475,9 +485,16 @@ class CFGConstraintBatch:
         making the copy: row b reads ``src[src_rows[b]]`` (any float dtype;
         rows 0..B-1 when ``src_rows`` is None), the masked fp32 row goes to
         ``out[b]`` (None: nowhere), ``src`` is not modified."""
+        return self._step_from_slots(self._slots(seq_ids), src, src_rows, out, neg_inf,
+                                     chunks_per_row)
+
+    def _step_from_slots(self, slots: torch.Tensor, src: torch.Tensor,
+                         src_rows: torch.Tensor | None, out: torch.Tensor | None,
+                         neg_inf: float = float("-inf"), chunks_per_row: int = 0,
+                         ) -> torch.Tensor:
+        """:meth:`step_greedy_from` on device slot indices (int64)."""
         from ..ops import _ptr, _source_args
 
-        slots = self._slots(seq_ids)
         B = int(slots.numel())
         code, rows, out = _source_args(src, self.g.vocab_size, B, src_rows, out, self.device)
         tokens = torch.empty(B, dtype=torch.int64, device=self.device)
