@@ -19,6 +19,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libbpd_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libbpdref.so")
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libbpdref_cuda.so")
 
 NCFG = 266
 
@@ -290,3 +291,107 @@ def argmax_rows(x: np.ndarray) -> np.ndarray:
     """torch.argmax(-1) semantics on float rows: first maximal index, NaN is
     maximal (numpy's argmax has the same rules)."""
     return np.argmax(x, axis=1).astype(np.int64)
+
+
+class _RefPdaStruct(C.Structure):
+    """ref_cuda_shim.cu's RefPda."""
+
+    _fields_ = [
+        ("num_states", _I), ("root_start", _I), ("root_accept", _I),
+        ("accept", _P), ("live", _P), ("edge_offsets", _P), ("edge_kind", _P),
+        ("edge_lo", _P), ("edge_hi", _P), ("edge_dst", _P), ("edge_callee", _P),
+        ("vocab_size", _I), ("eos_id", _I), ("tok_offsets", _P), ("tok_bytes", _P),
+    ]
+
+
+class RefCudaLib:
+    """The reference's own CUDA implementation (mask_cuda.cu, pda_cuda.cu),
+    compiled from its sources for sm_100a. Takes and returns torch CUDA
+    tensors; launches on the current stream without synchronising."""
+
+    def __init__(self) -> None:
+        lib = self.lib = _load(REF_CUDA_SO)
+        lib.bpdref_cuda_config_bytes.restype = _I
+        assert lib.bpdref_cuda_config_bytes() == NCFG * 4
+
+    @staticmethod
+    def available() -> bool:
+        return os.path.exists(REF_CUDA_SO)
+
+    @staticmethod
+    def _stream():
+        import torch
+
+        return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    @staticmethod
+    def _pda(g) -> _RefPdaStruct:
+        nedges = int(g.edge_kind.numel())
+        p = lambda t, n: C.c_void_p(t.data_ptr() if n else 0)  # noqa: E731
+        return _RefPdaStruct(
+            g.num_states, g.root_start, g.root_accept, p(g.accept, 1), p(g.live, 1),
+            p(g.edge_offsets, 1), p(g.edge_kind, nedges), p(g.edge_lo, nedges),
+            p(g.edge_hi, nedges), p(g.edge_dst, nedges), p(g.edge_callee, nedges),
+            g.vocab_size, g.eos_id, p(g.tok_offsets, 1), p(g.tok_bytes, 1))
+
+    def pda_mask(self, g, configs):
+        """Packed allow bits int32 [B, ceil(V/32)] (compute_mask_pda_batch_cuda)."""
+        import torch
+
+        B = int(configs.shape[0])
+        out = torch.empty((B, (g.vocab_size + 31) // 32), dtype=torch.int32,
+                          device=configs.device)
+        gs = self._pda(g)
+        self.lib.bpdref_cuda_pda_mask(C.byref(gs), C.c_void_p(configs.data_ptr()), _I(B),
+                                      C.c_void_p(out.data_ptr()), self._stream())
+        return out
+
+    def pda_apply_mask(self, g, configs, logits, neg_inf: float = float("-inf")) -> None:
+        """In place on fp32 logits [B, V] (apply_mask_pda_batch_cuda)."""
+        gs = self._pda(g)
+        self.lib.bpdref_cuda_pda_apply_mask(C.byref(gs), C.c_void_p(configs.data_ptr()),
+                                            _I(int(configs.shape[0])),
+                                            C.c_void_p(logits.data_ptr()), _F(neg_inf),
+                                            self._stream())
+
+    def pda_advance(self, g, configs, tokens):
+        """Advance configs [B, 266] in place by int32 tokens; uint8 ok [B]."""
+        import torch
+
+        B = int(configs.shape[0])
+        ok = torch.empty(B, dtype=torch.uint8, device=configs.device)
+        gs = self._pda(g)
+        self.lib.bpdref_cuda_pda_advance(C.byref(gs), C.c_void_p(configs.data_ptr()),
+                                         C.c_void_p(tokens.data_ptr()), _I(B),
+                                         C.c_void_p(ok.data_ptr()), self._stream())
+        return ok
+
+    def _fsa(self, f):
+        sym = f.symbols if f.symbols.numel() else f.offsets  # never read when empty
+        return (_I(int(f.accept.numel())), _I(f.num_symbols), C.c_void_p(f.trans.data_ptr()),
+                C.c_void_p(f.accept.data_ptr()), C.c_void_p(f.live.data_ptr()), _I(f.dead),
+                C.c_void_p(f.offsets.data_ptr()), C.c_void_p(sym.data_ptr()),
+                _I(int(f.offsets.numel()) - 1), _I(f.eos_id))
+
+    def compute_mask(self, f, states):
+        """Packed allow bits int32 [B, ceil(V/32)] of a byte-walk FSA
+        (compute_mask_batch_cuda); `f` an FsaTensors on the device."""
+        import torch
+
+        B = int(states.numel())
+        V = int(f.offsets.numel()) - 1
+        out = torch.empty((B, (V + 31) // 32), dtype=torch.int32, device=states.device)
+        self.lib.bpdref_cuda_compute_mask(*self._fsa(f), C.c_void_p(states.data_ptr()), _I(B),
+                                          C.c_void_p(out.data_ptr()), self._stream())
+        return out
+
+    def advance_state(self, f, states, tokens):
+        """Next states int32 [B] (advance_state_batch_cuda)."""
+        import torch
+
+        B = int(states.numel())
+        out = torch.empty(B, dtype=torch.int32, device=states.device)
+        self.lib.bpdref_cuda_advance_state(*self._fsa(f), C.c_void_p(states.data_ptr()),
+                                           C.c_void_p(tokens.data_ptr()), _I(B),
+                                           C.c_void_p(out.data_ptr()), self._stream())
+        return out
