@@ -304,53 +304,65 @@ __device__ __forceinline__ uint64_t fmix64(uint64_t x) {
   return x;
 }
 
-// Hash of the live content (num_configs, depths, frames); position-tagged so
-// config order matters, as it does for the mask under saturation.
+// Word k of the canonical form of config-set c: the live content (number of
+// configs, their depths and frames) with `saturated` and every word outside
+// the live region zero. Memo keys are stored in this form, so two sets have
+// the same mask key iff their canonical words are equal.
+__device__ __forceinline__ int32_t canon_word(const int32_t* c, int k) {
+  const int n = c[0];
+  if (k == 0) return n;
+  if (k == 1) return 0;
+  if (k < 2 + MC) return (k - 2) < n ? c[k] : 0;
+  const int i = (k - 2 - MC) / MD, f = (k - 2 - MC) % MD;
+  return (i < n && f < c[2 + i]) ? c[k] : 0;
+}
+
+constexpr int kRowWords = (NCFG + 31) / 32;  // words of a config row per lane
+
+// Warp-wide copy of a config row into shared memory: every load is issued
+// before the first store (one memory round trip, 128-byte coalesced).
+__device__ __forceinline__ void w_load_row(const int32_t* __restrict__ src, int32_t* dst,
+                                           int lane) {
+  int32_t v[kRowWords];
+#pragma unroll
+  for (int j = 0; j < kRowWords; ++j) {
+    const int k = lane + 32 * j;
+    v[j] = k < NCFG ? src[k] : 0;
+  }
+#pragma unroll
+  for (int j = 0; j < kRowWords; ++j) {
+    const int k = lane + 32 * j;
+    if (k < NCFG) dst[k] = v[j];
+  }
+  __syncwarp();
+}
+
+// Hash of the canonical form (position-tagged words; config order matters,
+// as it does for the mask under saturation).
 __device__ uint64_t w_hash(const int32_t* c, int lane) {
-  const int n = n_of(c);
   uint64_t h = 0;
-  for (int i = 0; i < n; ++i) {
-    const int d = c[2 + i];
-    if (lane < d)
-      h ^= fmix64((static_cast<uint64_t>(i * 32 + lane + 1) << 32) ^
-                  static_cast<uint32_t>(st_of(c, i)[lane]));
-    if (lane == 0) h ^= fmix64(0x5bd1e9955bd1e995ULL ^ (static_cast<uint64_t>(i) << 40) ^
-                               static_cast<uint32_t>(d));
+#pragma unroll
+  for (int j = 0; j < kRowWords; ++j) {
+    const int k = lane + 32 * j;
+    const int32_t v = k < NCFG ? canon_word(c, k) : 0;
+    if (v != 0) h ^= fmix64((static_cast<uint64_t>(k + 1) << 32) ^ static_cast<uint32_t>(v));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) h ^= __shfl_xor_sync(kAll, h, o);
-  return fmix64(h ^ static_cast<uint64_t>(n) * 0x9E3779B97F4A7C15ULL);
+  return fmix64(h);
 }
 
-// Live-content equality of two config-sets.
-__device__ bool w_same(const int32_t* a, const int32_t* b, int lane) {
-  const int n = n_of(a);
-  if (n != n_of(b)) return false;
-  for (int i = 0; i < n; ++i) {
-    const int d = a[2 + i];
-    if (d != b[2 + i]) return false;
-    const bool eq = lane >= d || st_of(a, i)[lane] == st_of(b, i)[lane];
-    if (!__all_sync(kAll, eq)) return false;
+// Same live content: config-set `a` (shared memory) against canonical words
+// held by each lane (key[j] = canonical word lane + 32 j of the other set).
+__device__ __forceinline__ bool w_same_words(const int32_t* a, const int32_t (&key)[kRowWords],
+                                             int lane) {
+  bool eq = true;
+#pragma unroll
+  for (int j = 0; j < kRowWords; ++j) {
+    const int k = lane + 32 * j;
+    if (k < NCFG) eq &= canon_word(a, k) == key[j];
   }
-  return true;
-}
-
-// Canonical form: live content, `saturated` and everything else zero.
-__device__ void w_canonical(const int32_t* src, int32_t* dst, int lane) {
-  const int n = n_of(src);
-  for (int k = lane; k < NCFG; k += 32) {
-    int32_t v = 0;
-    if (k == 0) {
-      v = n;
-    } else if (k >= 2 && k < 2 + MC) {
-      v = (k - 2) < n ? src[k] : 0;
-    } else if (k >= 2 + MC) {
-      const int i = (k - 2 - MC) / MD, f = (k - 2 - MC) % MD;
-      v = (i < n && f < src[2 + i]) ? src[k] : 0;
-    }
-    dst[k] = v;
-  }
-  __syncwarp();
+  return __all_sync(kAll, eq);
 }
 
 __device__ __forceinline__ int64_t slot_of(const int64_t* slots, int32_t b) {
@@ -360,26 +372,29 @@ __device__ __forceinline__ int64_t slot_of(const int64_t* slots, int32_t b) {
 // ---------------------------------------------------------------------------
 // Mask pipeline.
 
-// One warp per row: memo lookup and in-batch dedup. A row whose content is
-// neither in the memo nor already claimed by an equal row of this call
-// becomes a representative: it is appended to the representative list and
-// its first-byte table is cleared for the first-byte phase.
+// One warp per row, its config-set copied once into shared memory `A` (`B`:
+// scratch for a dedup comparison): memo lookup and in-batch dedup. A row
+// whose content is neither in the memo nor already claimed by an equal row of
+// this call becomes a representative: it is appended to the representative
+// list and its first-byte table is cleared for the first-byte phase.
 __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
                                            const int32_t* __restrict__ pool,
                                            const int64_t* __restrict__ slots,
                                            const uint8_t* __restrict__ broken, int32_t b,
-                                           const Memo& memo, const Work& w) {
+                                           const Memo& memo, const Work& w, int32_t* A,
+                                           int32_t* B) {
   const int lane = threadIdx.x & 31;
   const int64_t slot = slot_of(slots, b);
-  if (broken && broken[slot]) {
+  const bool brk = broken != nullptr && broken[slot] != 0;
+  w_load_row(pool + slot * NCFG, A, lane);
+  if (brk) {
     if (lane == 0) {
       w.kind[b] = kBroken;
       w.ref[b] = -1;
     }
     return;
   }
-  const int32_t* base = pool + slot * NCFG;
-  const uint64_t h = w_hash(base, lane);
+  const uint64_t h = w_hash(A, lane);
   int32_t kind = kRep, ref = -1;
   uint32_t cur = 0;  // this call's tag
   if (memo.cap) {
@@ -388,13 +403,22 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
   }
   // memo: entries claimed earlier in this call (tag == cur) are still being
   // filled and are skipped; equal content claimed by this call is found
-  // through the in-batch dedup below instead
+  // through the in-batch dedup below instead. An entry's tag, hash and key
+  // words are loaded together (one round trip per probe).
   for (int p = 0; memo.cap && p < kProbe; ++p) {
     const int32_t e = static_cast<int32_t>((h + p) & (memo.cap - 1));
+    const int32_t* key = memo.key + static_cast<int64_t>(e) * NCFG;
     const uint32_t tag = memo.tag[e];
+    const uint64_t eh = memo.hash[e];
+    int32_t kw[kRowWords];
+#pragma unroll
+    for (int j = 0; j < kRowWords; ++j) {
+      const int k = lane + 32 * j;
+      kw[j] = k < NCFG ? key[k] : 0;
+    }
     if (tag == 0u) break;
     if (tag == cur) continue;
-    if (memo.hash[e] == h && w_same(base, memo.key + static_cast<int64_t>(e) * NCFG, lane)) {
+    if (eh == h && w_same_words(A, kw, lane)) {
       kind = kHit;
       ref = e;
       break;
@@ -402,7 +426,8 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
   }
   if (kind != kHit) {
     // in-batch dedup: the first row to claim a dedup slot for this content is
-    // the representative; equal rows become its aliases
+    // the representative; equal rows become its aliases (compared on the
+    // other row's pool content, which this call never writes)
     for (int p = 0; p < w.dcap; ++p) {
       const int32_t d = static_cast<int32_t>((h + p) & (w.dcap - 1));
       int32_t prev = 0;
@@ -410,8 +435,14 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
       prev = __shfl_sync(kAll, prev, 0);
       if (prev == 0) break;  // representative
       const int32_t other = prev - 1;
-      const int32_t* orow = pool + slot_of(slots, other) * NCFG;
-      if (w_same(base, orow, lane)) {
+      w_load_row(pool + slot_of(slots, other) * NCFG, B, lane);
+      int32_t ow[kRowWords];
+#pragma unroll
+      for (int j = 0; j < kRowWords; ++j) {
+        const int k = lane + 32 * j;
+        ow[j] = k < NCFG ? canon_word(B, k) : 0;
+      }
+      if (w_same_words(A, ow, lane)) {
         kind = kAlias;
         ref = other;
         break;
@@ -422,7 +453,7 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
     if (lane < 8) w.first[static_cast<int64_t>(b) * 8 + lane] = 0u;
     if (lane == 0) {
       w.reps[atomicAdd(w.counters + 0, 1)] = b;
-      w.eos_ok[b] = is_complete(g, base) ? 1 : 0;
+      w.eos_ok[b] = is_complete(g, A) ? 1 : 0;
     }
     // claim a memo entry (none free along the probe: bits go to the workspace)
     for (int p = 0; memo.cap && p < kProbe; ++p) {
@@ -431,7 +462,8 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
       if (lane == 0) prev = atomicCAS(memo.tag + e, 0u, cur);
       prev = __shfl_sync(kAll, prev, 0);
       if (prev == 0u) {
-        w_canonical(base, memo.key + static_cast<int64_t>(e) * NCFG, lane);
+        int32_t* key = memo.key + static_cast<int64_t>(e) * NCFG;
+        for (int k = lane; k < NCFG; k += 32) key[k] = canon_word(A, k);
         if (lane == 0) memo.hash[e] = h;
         ref = e;
         break;
@@ -561,8 +593,10 @@ __global__ void __launch_bounds__(kLookupWarps * 32)
     lookup_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
                   const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
                   int32_t batch, Memo memo, Work w) {
-  const int32_t b = blockIdx.x * kLookupWarps + (threadIdx.x >> 5);
-  if (b < batch) lookup_row(g, pool, slots, broken, b, memo, w);
+  __shared__ int32_t buf[kLookupWarps][2][NCFG];
+  const int warp = threadIdx.x >> 5;
+  const int32_t b = blockIdx.x * kLookupWarps + warp;
+  if (b < batch) lookup_row(g, pool, slots, broken, b, memo, w, buf[warp][0], buf[warp][1]);
 }
 
 __global__ void __launch_bounds__(kThreads)
