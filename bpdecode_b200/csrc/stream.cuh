@@ -302,11 +302,11 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
         }
         issued = issued || row != nullptr;
       }
-      if constexpr (!kSoft && kArgmax && BPD_PIPELINE) {
+      if constexpr (!kSoft && BPD_PIPELINE) {
         // Software-pipelined live tiles: while tile t is blended, stored and
-        // folded vector by vector, the loads of tile t + 1 (when live) are
-        // issued into the registers each vector frees, so the argmax fold
-        // overlaps the next tile's memory latency.
+        // (with the argmax) folded vector by vector, the loads of tile t + 1
+        // (when live) are issued into the registers each vector frees, so
+        // this tile's work overlaps the next tile's memory latency.
         uint4 val[kVPT];
         bool loaded = false;  // val holds the current tile (warp-uniform)
 #pragma unroll
@@ -524,16 +524,20 @@ struct DenseCommit {
   }
 };
 
-// Register cap (resident CTAs per SM) and warp tiles per warp of a CTA;
-// tuned on B200 (8 resident CTAs beat fewer CTAs with more registers).
+// Register cap (resident CTAs per SM) and warp tiles per warp of a CTA,
+// tuned on B200: every streaming kernel runs at 48 registers (5 CTAs of 256
+// threads per SM) rather than 32 (8 CTAs). Against 8 CTAs at 32 registers:
+// fused dense step -11 % in late steps (the pipelined tile loop), mask-only
+// launches -5 % over a config-2 generation (pipelined too; +11 % on the first
+// step alone), fused soft step -7 % over a generation, soft apply -7 %.
 #ifndef BPD_APPLY_MIN_BLOCKS
-#define BPD_APPLY_MIN_BLOCKS 8
+#define BPD_APPLY_MIN_BLOCKS 5
 #endif
 #ifndef BPD_STEP_MIN_BLOCKS
-#define BPD_STEP_MIN_BLOCKS 5  // 48 registers: the pipelined step loop (8 CTAs at 32: -11 %)
+#define BPD_STEP_MIN_BLOCKS 5
 #endif
 #ifndef BPD_SOFT_STEP_MIN_BLOCKS
-#define BPD_SOFT_STEP_MIN_BLOCKS 8
+#define BPD_SOFT_STEP_MIN_BLOCKS 5
 #endif
 #ifndef BPD_TILES_PER_WARP
 #define BPD_TILES_PER_WARP 4
