@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from conftest import PDA_VOCAB, golden_npz
-from oracle.oracle import NCFG, HostPda, Oracle, RefLib
+from oracle.oracle import HostPda, Oracle, RefLib
 
 pytestmark = pytest.mark.gpu
 
