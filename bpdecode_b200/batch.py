@@ -245,9 +245,10 @@ class ConstraintBatch:
         """The bookkeeping of :meth:`add_many` (slots taken, grammars recorded)
         without the device write: returns the slots and the start state each
         must be given."""
-        if len(gs) != len(seq_ids) or len(set(seq_ids)) != len(seq_ids):
+        ids = set(seq_ids)
+        if len(gs) != len(seq_ids) or len(ids) != len(seq_ids):
             raise ValueError("add_many: one grammar per id, ids distinct")
-        if any(s in self._slot_of for s in seq_ids):
+        if not self._slot_of.keys().isdisjoint(ids):
             raise KeyError("add_many: a sequence is already in the batch")
         if len(seq_ids) > len(self._free):
             raise RuntimeError("ConstraintBatch is at capacity")

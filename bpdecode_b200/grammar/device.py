@@ -364,7 +364,8 @@ class CFGConstraintBatch:
     def _add_host(self, seq_ids: Sequence[Hashable]) -> list[int]:
         """The bookkeeping of :meth:`add_many` without the device write (the
         slots returned must get :meth:`_init_slots`)."""
-        if len(set(seq_ids)) != len(seq_ids) or any(s in self._slot_of for s in seq_ids):
+        ids = set(seq_ids)
+        if len(ids) != len(seq_ids) or not self._slot_of.keys().isdisjoint(ids):
             raise KeyError("add_many: ids must be distinct and new")
         if len(seq_ids) > len(self._free):
             raise RuntimeError("CFGConstraintBatch is at capacity")
@@ -377,7 +378,8 @@ class CFGConstraintBatch:
     def _init_slots(self, idx: torch.Tensor) -> None:
         """Fresh initial config-sets and cleared broken flags at device slot
         indices ``idx`` (int64)."""
-        self._configs.index_copy_(0, idx, self.g.init_batch(int(idx.numel())))
+        n = int(idx.numel())
+        self._configs.index_copy_(0, idx, self.g.init_config().unsqueeze(0).expand(n, -1))
         self._broken.index_fill_(0, idx, False)
 
     def evict_many(self, seq_ids: Sequence[Hashable]) -> None:
