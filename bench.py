@@ -37,6 +37,9 @@ SIGMA = 2.0
 # such episodes, every row restarting from its pattern's start state each
 # EPISODE steps (ConstraintBatch.reset_many, one device write).
 EPISODE = 128
+# Launches of the timed region bracketed by CUDA events for the step kernel's
+# duration (roofline.kernel_ms); 8 gives 16 launches of every generation.
+KERNEL_SAMPLE = 8
 METRIC = "constrained row-steps/sec (mask+apply+commit)"
 UNIT = "row-steps/s"
 # Algorithmic bytes of one row-step (bf16 logits, V = 128,256): logits read +
@@ -454,8 +457,13 @@ def main() -> None:
     barrier()
 
     stream = torch.cuda.current_stream(device)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+    # the step kernel's launch duration: CUDA events around every
+    # KERNEL_SAMPLE-th launch of the timed region (a pair of event records
+    # between two launches costs ~5 us of the step, so the others run back to
+    # back; the sampled launches stride evenly through every generation)
+    sampled = [i for i in range(args.steps) if i % KERNEL_SAMPLE == 0]
+    ev = {i: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for i in sampled}
     t_all0 = torch.cuda.Event(enable_timing=True)
     t_all1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -464,14 +472,17 @@ def main() -> None:
         for i in range(args.steps):
             if i and i % EPISODE == 0:
                 batch.reset_many(ids)
-            ev[i][0].record(stream)
+            pair = ev.get(i)
+            if pair is not None:
+                pair[0].record(stream)
             batch.step_greedy(ids, bufs[(i % EPISODE) % ring])
-            ev[i][1].record(stream)
+            if pair is not None:
+                pair[1].record(stream)
         t_all1.record(stream)
         torch.cuda.synchronize()
     barrier()
     elapsed_ms = t_all0.elapsed_time(t_all1)
-    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev)
+    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev.values())
     rank_ms = shard.gather_over_ranks(elapsed_ms, device)
     elapsed_ms, kern_ms = shard.max_over_ranks([elapsed_ms, kern_ms], device)
 
@@ -526,6 +537,10 @@ def main() -> None:
                      "kernel": "stream_step_kernel<bf16, DenseRows, DenseCommit> (fused "
                                "mask + argmax + commit)",
                      "kernel_ms": kern_ms,
+                     "kernel_timing": f"CUDA events around every {KERNEL_SAMPLE}th launch of "
+                                      f"the timed region ({len(sampled)} of {args.steps}), "
+                                      "each from before its launch to after it, launch "
+                                      "latency included",
                      "algo_bytes_per_row_step": ALGO_BYTES_PER_ROW_STEP},
         "clocks": clocks.summary(),
         "rank_ms": rank_ms,
