@@ -512,6 +512,10 @@ def main() -> None:
     torch.cuda.synchronize()
     un_ms = u0.elapsed_time(u1) / un_steps
 
+    # greedy without the masked logits: step_greedy_from with no output reads
+    # the allowed vectors, commits the argmax and writes nothing back
+    tokens_only = _tokens_only(batch, ids, bufs, ring, stream)
+
     # reference GPU bar: bpdecode's dense torch composite on this B200
     batch.reset_many(ids)
     ref_gpu = _reference_torch_gpu(batch, bufs, ring, device)
@@ -549,6 +553,7 @@ def main() -> None:
         "unfused_dropin": {"ms_per_step": un_ms, "value": ROWS_PER_GPU * world / (un_ms / 1e3),
                            "path": "ConstraintBatch.apply_mask + torch.argmax + commit"},
         "reference_torch_gpu": ref_gpu,
+        "tokens_only": tokens_only,
     }
     if not args.no_extra:
         # free the dense ring before the other workloads
@@ -754,6 +759,31 @@ def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 12
             "fused_logits_gbs": logit_bytes / (us_fused / 1e6) / 1e9,
             "note": "fused_logits_gbs counts the logits read + written once per step "
                     "(2 x 4 B x V per row); rejected tiles are written without a read"}
+
+
+def _tokens_only(batch, ids, bufs, ring, stream) -> dict:
+    """ConstraintBatch.step_greedy_from(ids, logits) with no output: the same
+    mask + argmax + commit of every row on the config-2 trajectory, but the
+    masked logits are not materialised (a sampler that needs only the greedy
+    token). Logits are read where a token is allowed and never written. One
+    generation of 128 steps, CUDA events around the whole run."""
+    for i in range(3):
+        batch.step_greedy_from(ids, bufs[i % ring])
+    batch.reset_many(ids)
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(EPISODE):
+        batch.step_greedy_from(ids, bufs[i % ring])
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / EPISODE
+    batch.reset_many(ids)
+    return {"ms_per_step": ms, "value": ROWS_PER_GPU / (ms / 1e3),
+            "algo_bytes_per_row_step": V * E + 4 * ((V + 31) // 32) + 16,
+            "path": "ConstraintBatch.step_greedy_from(ids, bf16 logits) -- tokens and commits, "
+                    "no masked logits written"}
 
 
 def _reference_torch_gpu(batch, bufs, ring, device) -> dict:
