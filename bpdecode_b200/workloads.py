@@ -122,11 +122,6 @@ def vocab_large(size: int = 128_256, seed: int = 0) -> Vocabulary:
     return Vocabulary(tuple(out), eos_id=size - 1)
 
 
-def token_id(vocab: Vocabulary, tok: bytes) -> int:
-    """Lowest id whose bytes equal ``tok``."""
-    return vocab.token_bytes.index(tok)
-
-
 def row_patterns(batch: int, seed: int = 0, n_patterns: int = len(DENSE_PATTERNS)) -> list[int]:
     """Pattern index per row, uniform from the seed (config 2)."""
     rng = random.Random(seed * 104729 + batch)

@@ -287,12 +287,6 @@ def dfa_with_vocab(dfa: dict, token_bytes: tuple[bytes, ...]) -> tuple[np.ndarra
     return offsets, lut[flat].astype(np.int32)
 
 
-def argmax_rows(x: np.ndarray) -> np.ndarray:
-    """torch.argmax(-1) semantics on float rows: first maximal index, NaN is
-    maximal (numpy's argmax has the same rules)."""
-    return np.argmax(x, axis=1).astype(np.int64)
-
-
 class _RefPdaStruct(C.Structure):
     """ref_cuda_shim.cu's RefPda."""
 

@@ -79,10 +79,3 @@ def vocab_of(vname: str):
 
     toks, eos = VOCABS[vname]
     return Vocabulary.from_tokens(toks, eos_id=eos)
-
-
-def reference_src() -> str | None:
-    """bpdecode's source tree when it is present (only in the build container)."""
-    path = os.environ.get("BPDECODE_REFERENCE", "/root/reference")
-    src = os.path.join(path, "src")
-    return src if os.path.isdir(os.path.join(src, "bpdecode")) else None
