@@ -7,8 +7,11 @@ tokens, 1024 rows per GPU, each row constrained by one of 8 regexes (IPv4,
 date, e-mail, signed float, hex colour, UUID, name, phone) chosen from the
 seed, bf16 logits ~ N(0, 2), greedy (argmax) commit. A step is mask + apply +
 argmax + commit of every row: one fused launch per step
-(ConstraintBatch.step_greedy). Rows are sharded by request: every rank owns
-1024 rows and no collective runs on the hot path (weak scaling).
+(ConstraintBatch.step_greedy). Rows are sharded by request: the global rows
+are cut into blocks of 1024 (bpdecode_b200.workloads.ROW_BLOCK), rank r owns
+block r (shard.shard_rows), every row's pattern and logits depend only on its
+block, so rank r computes what one process over the global batch computes for
+those rows, and no collective runs on the hot path (weak scaling).
 
 Prints one JSON line (rank 0). Under torchrun each rank runs on LOCAL_RANK;
 timing is the max over ranks of CUDA-event time.
@@ -37,9 +40,6 @@ SIGMA = 2.0
 # such episodes, every row restarting from its pattern's start state each
 # EPISODE steps (ConstraintBatch.reset_many, one device write).
 EPISODE = 128
-# Launches of the timed region bracketed by CUDA events for the step kernel's
-# duration (roofline.kernel_ms); 8 gives 16 launches of every generation.
-KERNEL_SAMPLE = 8
 METRIC = "constrained row-steps/sec (mask+apply+commit)"
 UNIT = "row-steps/s"
 # Algorithmic bytes of one row-step (bf16 logits, V = 128,256): logits read +
@@ -63,18 +63,28 @@ def _peaks() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
-def _profile_traffic() -> float | None:
-    """DRAM bytes per launch of the fused step kernel from the committed ncu
-    summary (a line `traffic_bytes_per_launch: N`), if present."""
+def _profile_traffic(steps: int) -> tuple[float | None, str]:
+    """Mean DRAM bytes (read + write) per launch of the fused step kernel over
+    the generation steps a timed region of `steps` launches covers (step i of
+    the region is generation step i mod EPISODE), from the committed ncu
+    summary: one line `step_dram_bytes: <step> <read> <write>` per generation
+    step. (None, why) when the summary does not cover those steps."""
     path = os.path.join(ROOT, "profiles", "dense_step_config2.md")
+    per: dict[int, float] = {}
     try:
         with open(path) as f:
             for line in f:
-                if line.strip().startswith("traffic_bytes_per_launch:"):
-                    return float(line.split(":", 1)[1].strip().split()[0])
+                if line.strip().startswith("step_dram_bytes:"):
+                    k, rd, wr = line.split(":", 1)[1].split()[:3]
+                    per[int(k)] = float(rd) + float(wr)
     except OSError:
-        pass
-    return None
+        return None, "no ncu summary"
+    want = [i % EPISODE for i in range(steps)]
+    if not per or any(k not in per for k in want):
+        return None, "ncu summary does not cover the timed steps"
+    return statistics.fmean(per[k] for k in want), (
+        f"ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, mean over generation "
+        f"steps {min(want)}..{max(want)} (the steps this run timed), profiles/dense_step_config2.md")
 
 
 class ClockSampler:
@@ -135,16 +145,26 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def build_workload(rank: int, device: torch.device):
+def build_workload(block: int, device: torch.device):
+    """Tables of the 8 patterns and the pattern of every row of global row
+    block `block`."""
     from bpdecode_b200 import tables
-    from bpdecode_b200.batch import ConstraintBatch
     from bpdecode_b200.ops import FsaTensors
-    from bpdecode_b200.workloads import DENSE_PATTERNS, row_patterns, vocab_large
+    from bpdecode_b200.workloads import DENSE_PATTERNS, block_patterns, vocab_large
 
     vocab = vocab_large(V)
     fsas = [FsaTensors.from_arrays(tables.load_dfa(n), vocab).to(device)
             for n, _ in DENSE_PATTERNS]
-    return vocab, fsas, row_patterns(ROWS_PER_GPU, seed=rank)
+    return vocab, fsas, block_patterns(block, ROWS_PER_GPU)
+
+
+def my_block(rank: int, world: int) -> int:
+    """The global row block this rank owns (blocks of ROWS_PER_GPU rows)."""
+    from bpdecode_b200 import shard
+
+    rows = shard.shard_rows(ROWS_PER_GPU * world, world, rank)
+    assert len(rows) == ROWS_PER_GPU and rows.start % ROWS_PER_GPU == 0
+    return rows.start // ROWS_PER_GPU
 
 
 def make_batch(fsas, pats):
@@ -156,8 +176,11 @@ def make_batch(fsas, pats):
     return batch
 
 
-def gen_logits(rank: int, step: int, device: torch.device, out: torch.Tensor | None = None):
-    g = torch.Generator(device=device).manual_seed(rank * 1_000_003 + step)
+def gen_logits(block: int, step: int, device: torch.device, out: torch.Tensor | None = None):
+    """bf16 logits N(0, SIGMA^2) of global row block `block` at step `step`."""
+    from bpdecode_b200.workloads import block_logits_seed
+
+    g = torch.Generator(device=device).manual_seed(block_logits_seed(block, step))
     x = torch.randn(ROWS_PER_GPU, V, generator=g, device=device) * SIGMA
     if out is None:
         return x.to(torch.bfloat16)
@@ -165,35 +188,64 @@ def gen_logits(rank: int, step: int, device: torch.device, out: torch.Tensor | N
     return out
 
 
-def cpu_baseline(tok_next_cpu: torch.Tensor, starts: list[int], pats: list[int],
-                 rows: int, steps: int) -> dict:
-    """The reference's own dense torch step on host cores (all torch threads)."""
+def _cpu_tables(tns: list[torch.Tensor], starts_local: list[int]) -> tuple[torch.Tensor, list[int]]:
+    """The batch's global tok_next (grammars concatenated, state ids offset)
+    and start states, on the host."""
+    out, starts, off = [], [], 0
+    for tn, st in zip(tns, starts_local):
+        tn = tn.cpu()
+        out.append(torch.where(tn >= 0, tn + off, tn))
+        starts.append(st + off)
+        off += tn.shape[0]
+    return torch.cat(out), starts
+
+
+def _time_cpu_reference(tok_next: torch.Tensor, starts: list[int], pats: list[int],
+                        steps: int, warmup: int) -> float:
+    """Seconds for `steps` steps of the reference's dense step on host cores
+    over every row of the block (128-step generations from the start states,
+    as on the GPU), after `warmup` untimed steps. Four seeded bf16 logits
+    buffers of the workload's shape are cycled (the CPU arm masks them in
+    place, which leaves later steps' allowed tokens unchanged)."""
     from oracle import torch_port
 
-    torch.set_num_threads(len(os.sched_getaffinity(0)))
-    state = torch.tensor([starts[p] for p in pats[:rows]], dtype=torch.int32)
+    rows = len(pats)
+    state = torch.tensor([starts[p] for p in pats], dtype=torch.int32)
+    start = state.clone()
     slots = torch.arange(rows)
     g = torch.Generator().manual_seed(12345)
-    samples = [(torch.randn(rows, V, generator=g) * SIGMA).to(torch.bfloat16)
-               for _ in range(min(steps, 4))]
-    torch_port.step(samples[0], tok_next_cpu, state.clone(), slots)  # warm
-    start = state.clone()
+    pool = [(torch.randn(rows, V, generator=g) * SIGMA).to(torch.bfloat16) for _ in range(4)]
+    for i in range(warmup):
+        torch_port.step(pool[i % 4], tok_next, state, slots)
+    state.copy_(start)
     t0 = time.perf_counter()
     for i in range(steps):
         if i and i % EPISODE == 0:
             state.copy_(start)
-        torch_port.step(samples[i % len(samples)], tok_next_cpu, state, slots)
-    dt = time.perf_counter() - t0
+        torch_port.step(pool[i % 4], tok_next, state, slots)
+    return time.perf_counter() - t0
+
+
+_CPU_SAMPLE = ("every row of the {rows}-row block, bf16, V={V}: torch CPU restatement of "
+               "bpdecode's dense step (ops.py:271-276 mask, argmax, ops.py:301-306 commit; the "
+               "reference's dense path is torch, not compiled code), {steps} steps, {dt:.1f} s")
+
+
+def cpu_baseline(tok_next_cpu: torch.Tensor, starts: list[int], pats: list[int],
+                 steps: int) -> dict:
+    """The reference's own dense torch step on host cores (all torch threads),
+    a bounded sample of this workload: every row, `steps` steps."""
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    dt = _time_cpu_reference(tok_next_cpu, starts, pats, steps, 1)
+    rows = len(pats)
     return {"value": rows * steps / dt, "unit": UNIT, "cores": torch.get_num_threads(),
-            "kind": "port",
-            "sample": f"{rows} of the {ROWS_PER_GPU} rows x {steps} steps, bf16, V={V}, "
-                      "torch CPU restatement of ops.py:271-276/301-306 + argmax "
-                      f"({dt:.1f} s)"}
+            "kind": "port", "sample": _CPU_SAMPLE.format(rows=rows, V=V, steps=steps, dt=dt)}
 
 
 def run_reference(args: argparse.Namespace) -> None:
     """--impl reference: the reference's CPU implementation of the step, timed
-    on host cores on this workload; rank 0 only."""
+    on host cores on this arm's workload (the same 1024-row block, patterns,
+    vocabulary, dtype and generation length); rank 0 only."""
     rank, world, _ = _dist()
     if rank != 0:
         return
@@ -201,42 +253,21 @@ def run_reference(args: argparse.Namespace) -> None:
     # takes every host core it may use
     torch.set_num_threads(len(os.sched_getaffinity(0)))
     from bpdecode_b200 import tables
-    from bpdecode_b200.workloads import DENSE_PATTERNS, row_patterns, vocab_large
+    from bpdecode_b200.workloads import DENSE_PATTERNS, block_patterns, vocab_large
     from oracle.oracle import Oracle, dfa_with_vocab
 
     vocab = vocab_large(V)
     orc = Oracle()
-    tns, starts, off = [], [], 0
+    tns, starts_local = [], []
     for n, _ in DENSE_PATTERNS:
         d = tables.load_dfa(n)
-        o, s = dfa_with_vocab(d, vocab.token_bytes)
-        tn = torch.from_numpy(orc.build_tok_next(d, o, s, vocab.eos_id))
-        tns.append(torch.where(tn >= 0, tn + off, tn))
-        starts.append(d["start"] + off)
-        off += tn.shape[0]
-    tok_next = torch.cat(tns)
-    pats = row_patterns(ROWS_PER_GPU, seed=0)
-    rows = 256
-    state = torch.tensor([starts[p] for p in pats[:rows]], dtype=torch.int32)
-    slots = torch.arange(rows)
-    g = torch.Generator().manual_seed(12345)
-    pool = [(torch.randn(rows, V, generator=g) * SIGMA).to(torch.bfloat16) for _ in range(4)]
-    from oracle import torch_port
-
-    start = state.clone()
-    for i in range(args.warmup):
-        torch_port.step(pool[i % 4], tok_next, state, slots)
-    state.copy_(start)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        if i and i % EPISODE == 0:
-            state.copy_(start)
-        torch_port.step(pool[i % 4], tok_next, state, slots)
-    dt = time.perf_counter() - t0
-    value = rows * args.steps / dt
-    sample = (f"{rows} rows per step of the {ROWS_PER_GPU}-row workload, bf16, V={V}; torch "
-              "CPU restatement of bpdecode's dense step (ops.py:271-276/301-306 + argmax); "
-              "bpdecode's dense path is torch, not compiled code")
+        o, sy = dfa_with_vocab(d, vocab.token_bytes)
+        tns.append(torch.from_numpy(orc.build_tok_next(d, o, sy, vocab.eos_id)))
+        starts_local.append(d["start"])
+    tok_next, starts = _cpu_tables(tns, starts_local)
+    pats = block_patterns(0, ROWS_PER_GPU)
+    dt = _time_cpu_reference(tok_next, starts, pats, args.steps, args.warmup)
+    value = ROWS_PER_GPU * args.steps / dt
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -244,19 +275,23 @@ def run_reference(args: argparse.Namespace) -> None:
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": _config(world),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": sample},
+                         "kind": "port",
+                         "sample": _CPU_SAMPLE.format(rows=ROWS_PER_GPU, V=V, steps=args.steps,
+                                                      dt=dt)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def _config(world: int) -> dict:
+    """The workload, identical in both arms' lines."""
     return {
-        "workload": "dense regex step at serving scale: 8 regexes mixed per batch, "
+        "workload": "dense regex step at serving scale (config 2): 8 regexes mixed per batch, "
                     f"V={V}, {ROWS_PER_GPU} rows per GPU, bf16 logits N(0,{SIGMA:g}), argmax "
-                    f"commit, {EPISODE}-step generations (config 2)",
+                    f"commit, {EPISODE}-step generations from the start states",
         "vocab": V, "rows_per_gpu": ROWS_PER_GPU, "global_batch": ROWS_PER_GPU * world,
-        "parallelism": f"dp{world} (rows sharded by request, no collective)",
+        "parallelism": f"dp{world} (rows sharded by request in global blocks of "
+                       f"{ROWS_PER_GPU}, no collective)",
         "l2": "inputs larger than L2: every step reads a 262 MB logits buffer (126 MB L2)",
     }
 
@@ -439,12 +474,13 @@ def main() -> None:
     device = torch.device("cuda", local)
     shard.init("nccl", device)
 
-    vocab, fsas, pats = build_workload(rank, device)
+    block = my_block(rank, world)
+    vocab, fsas, pats = build_workload(block, device)
     batch = make_batch(fsas, pats)
     ids = list(range(ROWS_PER_GPU))
 
     ring = max(1, min(args.ring, args.steps + args.warmup))
-    bufs = [gen_logits(rank, i, device) for i in range(ring)]
+    bufs = [gen_logits(block, i, device) for i in range(ring)]
     torch.cuda.synchronize()
 
     barrier = shard.barrier
@@ -457,40 +493,61 @@ def main() -> None:
     barrier()
 
     stream = torch.cuda.current_stream(device)
-    # the step kernel's launch duration: CUDA events around every
-    # KERNEL_SAMPLE-th launch of the timed region (a pair of event records
-    # between two launches costs ~5 us of the step, so the others run back to
-    # back; the sampled launches stride evenly through every generation)
-    sampled = [i for i in range(args.steps) if i % KERNEL_SAMPLE == 0]
-    ev = {i: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for i in sampled}
+
+    def run_steps(pairs: list | None) -> None:
+        for i in range(args.steps):
+            if i and i % EPISODE == 0:
+                batch.reset_many(ids)
+            if pairs is not None:
+                pairs[i][0].record(stream)
+            batch.step_greedy(ids, bufs[(i % EPISODE) % ring])
+            if pairs is not None:
+                pairs[i][1].record(stream)
+
+    # the timed region: the launches back to back, nothing else on the stream
     t_all0 = torch.cuda.Event(enable_timing=True)
     t_all1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         t_all0.record(stream)
-        for i in range(args.steps):
-            if i and i % EPISODE == 0:
-                batch.reset_many(ids)
-            pair = ev.get(i)
-            if pair is not None:
-                pair[0].record(stream)
-            batch.step_greedy(ids, bufs[(i % EPISODE) % ring])
-            if pair is not None:
-                pair[1].record(stream)
+        run_steps(None)
         t_all1.record(stream)
         torch.cuda.synchronize()
     barrier()
     elapsed_ms = t_all0.elapsed_time(t_all1)
-    kern_ms = statistics.fmean(a.elapsed_time(b) for a, b in ev.values())
+
+    # the step kernel's duration per launch: the same trajectory again (rows
+    # back at their start states, the same logits buffers) with CUDA events
+    # around every launch. A 1 GiB fill enqueued first keeps the GPU busy
+    # while the first launches are issued, so every start event fires when
+    # the previous launch ends, not when the host records it: the pairs time
+    # the kernels, not the host's launch latency.
+    batch.reset_many(ids)
+    pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+             for _ in range(args.steps)]
+    busy = torch.empty(1 << 30, dtype=torch.uint8, device=device)
+    torch.cuda.synchronize()
+    busy.fill_(1)
+    run_steps(pairs)
+    torch.cuda.synchronize()
+    del busy
+    per_launch_ms = [a.elapsed_time(b) for a, b in pairs]
+    kern_ms = statistics.fmean(per_launch_ms)
     rank_ms = shard.gather_over_ranks(elapsed_ms, device)
     elapsed_ms, kern_ms = shard.max_over_ranks([elapsed_ms, kern_ms], device)
+    ms_per_step = elapsed_ms / args.steps
+    # one launch per step, so a kernel cannot take longer than a step (the
+    # tolerance covers the event records' own cost)
+    if kern_ms > ms_per_step * 1.02:
+        raise RuntimeError(f"kernel time {kern_ms:.4f} ms exceeds the step time "
+                           f"{ms_per_step:.4f} ms: the per-launch events are not timing "
+                           "the kernel")
 
     total_rows = ROWS_PER_GPU * world * args.steps
     value = total_rows / (elapsed_ms / 1000.0)
     peak, peak_kind = _peaks()
     achieved = ROWS_PER_GPU * ALGO_BYTES_PER_ROW_STEP / (kern_ms / 1000.0) / 1e9
-    traffic = _profile_traffic()
+    traffic, traffic_src = _profile_traffic(args.steps)
 
     # unfused drop-in path: apply_mask + torch.argmax + commit (3 launches),
     # the first 64 steps of an episode
@@ -522,30 +579,39 @@ def main() -> None:
 
     # end to end through the public API with host buffers
     batch.reset_many(ids)
-    e2e = _e2e(batch, ids, rank, device, args.e2e_steps, world)
+    e2e = _e2e(batch, ids, block, device, args.e2e_steps, world)
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {**_config(world), "logits_ring": ring, "episode_steps": EPISODE,
-                   "episodes": (args.steps + EPISODE - 1) // EPISODE,
-                   "ring_note": (f"every row restarts from its start state each {EPISODE} "
-                                 f"steps (one device write inside the timed region); step j "
-                                 f"of an episode reads buffer j mod {ring}, so every episode "
-                                 "replays the same trajectory (masking in place is idempotent)")},
+        "config": _config(world),
+        "timed_window": {"block": block, "logits_ring": ring, "episode_steps": EPISODE,
+                         "episodes": (args.steps + EPISODE - 1) // EPISODE,
+                         "note": (f"every row restarts from its start state each {EPISODE} "
+                                  f"steps (one device write inside the timed region); step j "
+                                  f"of an episode reads buffer j mod {ring}, so every episode "
+                                  "replays the same trajectory (masking in place is "
+                                  "idempotent)")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
+                     "traffic_source": traffic_src,
+                     "achieved_traffic_gbs": (traffic / (kern_ms / 1000.0) / 1e9
+                                              if traffic else None),
+                     "frac_traffic": (traffic / (kern_ms / 1000.0) / 1e9 / peak
+                                      if traffic else None),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                      if peak_kind == "measured" else "fallback 6.65 TB/s",
                      "kernel": "stream_step_kernel<bf16, DenseRows, DenseCommit> (fused "
                                "mask + argmax + commit)",
                      "kernel_ms": kern_ms,
-                     "kernel_timing": f"CUDA events around every {KERNEL_SAMPLE}th launch of "
-                                      f"the timed region ({len(sampled)} of {args.steps}), "
-                                      "each from before its launch to after it, launch "
-                                      "latency included",
-                     "algo_bytes_per_row_step": ALGO_BYTES_PER_ROW_STEP},
+                     "kernel_ms_first_last": [per_launch_ms[0], per_launch_ms[-1]],
+                     "kernel_timing": f"CUDA events around each of the {args.steps} launches "
+                                      "of a replay of the timed steps (same trajectory), the "
+                                      "GPU kept busy by a 1 GiB fill while the first launches "
+                                      "were issued; mean per launch, max over ranks",
+                     "algo_bytes_per_row_step": ALGO_BYTES_PER_ROW_STEP,
+                     "algo_bytes_per_launch": ROWS_PER_GPU * ALGO_BYTES_PER_ROW_STEP},
         "clocks": clocks.summary(),
         "rank_ms": rank_ms,
         "gpu_launches": args.steps,
@@ -563,13 +629,9 @@ def main() -> None:
         line["dense_config3"] = _dense_config3(device, rank)
         line["soft_lookahead"] = _soft_lookahead(fsas, pats, device, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        off, tns, starts = 0, [], []
-        for f in fsas:
-            tn = f.dense_tables()[0].cpu()
-            tns.append(torch.where(tn >= 0, tn + off, tn))
-            starts.append(f.start + off)
-            off += f.num_states
-        line["cpu_baseline"] = cpu_baseline(torch.cat(tns), starts, pats, 256, 320)
+        tok_next, starts = _cpu_tables([f.dense_tables()[0] for f in fsas],
+                                       [f.start for f in fsas])
+        line["cpu_baseline"] = cpu_baseline(tok_next, starts, pats, 80)
     if rank == 0:
         print(json.dumps(line), flush=True)
     shard.finish()
@@ -819,14 +881,14 @@ def _reference_torch_gpu(batch, bufs, ring, device) -> dict:
             "path": "ops.py dense composite (index_select + masked_fill_ + argmax + gather)"}
 
 
-def _e2e(batch, ids, rank, device, steps, world) -> dict:
-    from bpdecode_b200 import shard
-
+def _e2e(batch, ids, block, device, steps, world) -> dict:
     """Same step through the public API from pinned host logits: every step
     copies its logits host -> device, runs ConstraintBatch.step_greedy and
     reads the chosen tokens back."""
+    from bpdecode_b200 import shard
+
     nhost = 2
-    host = [gen_logits(rank, 10_000 + i, device).cpu().pin_memory() for i in range(nhost)]
+    host = [gen_logits(block, 10_000 + i, device).cpu().pin_memory() for i in range(nhost)]
     dev = torch.empty(ROWS_PER_GPU, V, dtype=torch.bfloat16, device=device)
     out = torch.empty(ROWS_PER_GPU, dtype=torch.int64).pin_memory()
     for i in range(2):

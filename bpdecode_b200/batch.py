@@ -20,7 +20,7 @@ changes is underneath:
 
 from __future__ import annotations
 
-from collections import OrderedDict, defaultdict
+from collections import OrderedDict
 from collections.abc import Hashable, Sequence
 
 import torch
@@ -42,75 +42,103 @@ FREE = -2  # slot holds no sequence
 BROKEN = -1  # a committed token left the grammar-valid path
 
 
-class MaskCache:
-    """LRU cache of allow-sets keyed by DFA state (batch.py:35-86).
+_BIT_SHIFTS: dict[torch.device, torch.Tensor] = {}
 
-    Kept for API compatibility: with the packed allow rows resident on the
-    device, the uncached kernel path is already a per-state lookup, so the
-    cache no longer saves work -- it returns identical logits.
+
+def _unpack_allow_row(words: torch.Tensor, vocab: int) -> torch.Tensor:
+    """Token ids (int64, ascending) whose bit is set in one packed allow row
+    (int32 storage of uint32 words, bit t of word t >> 5)."""
+    shifts = _BIT_SHIFTS.get(words.device)
+    if shifts is None:
+        shifts = torch.arange(32, dtype=torch.int32, device=words.device)
+        _BIT_SHIFTS[words.device] = shifts
+    flags = (words.unsqueeze(1) >> shifts).bitwise_and_(1).reshape(-1)[:vocab]
+    return flags.nonzero().reshape(-1)
+
+
+class MaskCache:
+    """Allow-sets of one dense grammar, per DFA state (API of batch.py:35-86).
+
+    On this device path every state's allow-set is already resident as a
+    packed bit row (``FsaTensors.allow_bits``), 32x smaller than the id
+    list, and masking a batch is one kernel launch whatever the states. So
+    this class keeps no copy of the masks: :meth:`apply` is that launch, and
+    :meth:`allowed_ids` unpacks one state's row into token ids on demand,
+    remembering the ``max_states`` most recently requested lists. States that
+    :meth:`apply` masks with count as held (``len``) from the next query on;
+    :meth:`apply` itself does not synchronise with the device.
     """
 
     def __init__(self, fsa: FsaTensors, max_states: int = 512) -> None:
         self._fsa = fsa
-        self._vocab = int(fsa.offsets.numel() - 1)
         self._max = max_states
-        self._allowed: OrderedDict[int, torch.Tensor] = OrderedDict()
+        # state -> unpacked ids (None until asked for); dict order = recency
+        self._allowed: dict[int, torch.Tensor | None] = {}
+        self._pending: list[torch.Tensor] = []  # state tensors of apply() calls
 
-    def _compute(self, state: int) -> torch.Tensor:
-        probe = torch.zeros(1, self._vocab, device=self._fsa.device)
-        st = torch.tensor([state], dtype=torch.int32, device=self._fsa.device)
-        apply_mask_(probe, self._fsa, st)
-        return (probe[0] == 0.0).nonzero(as_tuple=False).squeeze(1).to(torch.long)
+    def _remember(self, state: int, ids: torch.Tensor | None) -> None:
+        known = self._allowed.pop(state, None)
+        self._allowed[state] = ids if ids is not None else known
+        while len(self._allowed) > self._max:
+            del self._allowed[next(iter(self._allowed))]
+
+    def _settle(self) -> None:
+        """Fold the states of earlier apply() calls into the recency order."""
+        pending, self._pending = self._pending, []
+        for st in pending:
+            for s in torch.unique(st).tolist():
+                self._remember(int(s), None)
 
     def allowed_ids(self, state: int) -> torch.Tensor:
-        hit = self._allowed.get(state)
-        if hit is not None:
-            self._allowed.move_to_end(state)
-            return hit
-        ids = self._compute(state)
-        self._allowed[state] = ids
-        if len(self._allowed) > self._max:
-            self._allowed.popitem(last=False)
+        self._settle()
+        ids = self._allowed.get(state)
+        if ids is None:
+            _, bits = self._fsa.dense_tables()
+            if 0 <= state < self._fsa.num_states:
+                ids = _unpack_allow_row(bits[state], self._fsa.vocab_size)
+            else:
+                ids = torch.zeros(0, dtype=torch.long, device=bits.device)
+        self._remember(state, ids)
         return ids
 
     def __len__(self) -> int:
+        self._settle()
         return len(self._allowed)
 
     def apply(
         self, states: torch.Tensor, logits: torch.Tensor, neg_inf: float = float("-inf")
     ) -> torch.Tensor:
-        """In place: mask ``logits`` [n, vocab] given one state per row."""
-        by_state: dict[int, list[int]] = defaultdict(list)
-        for i, s in enumerate(states.tolist()):
-            by_state[s].append(i)
-        for state, rows in by_state.items():
-            allowed = self.allowed_ids(state).to(logits.device)
-            r = torch.tensor(rows, device=logits.device)
-            keep = logits.index_select(0, r).index_select(1, allowed)
-            logits[r] = neg_inf
-            logits[r.unsqueeze(1), allowed] = keep
+        """In place: mask ``logits`` [n, vocab] given one state per row (one
+        ``bpd_dense_apply_mask`` launch)."""
+        apply_mask_(logits, self._fsa, states, neg_inf)
+        self._pending.append(states.detach().reshape(-1))
         return logits
 
 
 class GrammarCache:
-    """LRU cache of compiled grammars for one tokenizer / device (batch.py:89-115)."""
+    """Compiled grammars for one tokenizer and device, shared by every
+    request that names the same pattern (API of batch.py:89-115).
+
+    ``get`` compiles a pattern (a regex string or a compiled DFA) the first
+    time it is asked for and returns the same :class:`FsaTensors` -- tables
+    already on ``device`` -- every later time; the ``max_size`` most recently
+    used grammars are kept.
+    """
 
     def __init__(self, vocab: object, device: torch.device | str = "cpu", max_size: int = 128,
                  ) -> None:
         self._vocab = vocab
         self._device = torch.device(device)
         self._max = max_size
-        self._cache: OrderedDict[str, FsaTensors] = OrderedDict()
+        self._cache: dict[Hashable, FsaTensors] = {}  # dict order = recency
 
-    def get(self, pattern: str) -> FsaTensors:
-        hit = self._cache.get(pattern)
-        if hit is not None:
-            self._cache.move_to_end(pattern)
-            return hit
-        fsa = FsaTensors.build(pattern, self._vocab).to(self._device)
+    def get(self, pattern: object) -> FsaTensors:
+        fsa = self._cache.pop(pattern, None)
+        if fsa is None:
+            fsa = FsaTensors.build(pattern, self._vocab).to(self._device)
         self._cache[pattern] = fsa
-        if len(self._cache) > self._max:
-            self._cache.popitem(last=False)
+        while len(self._cache) > self._max:
+            del self._cache[next(iter(self._cache))]
         return fsa
 
     def __len__(self) -> int:

@@ -35,6 +35,8 @@
 //   -> first_byte_kernel -> compute_kernel (misses only; both exit at once when
 //   every row hit) -> apply, or the fused step (apply + argmax, and the warp
 //   that finishes a row advances its config-set by the winning token).
+#include <cuda.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -989,10 +991,36 @@ __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[kMaxDevices] = {};
+CUcontext g_noalloc_ctx[kMaxDevices] = {};  // the context each address belongs to
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+
+// The calling thread's current driver context (nullptr if it has none yet),
+// through the driver entry point the runtime hands out, so the library does
+// not link libcuda itself.
+bpd_status current_context(CUcontext* ctx) {
+  if (g_ctx_get_current == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    const cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return fail(BPD_ERR_CUDA, "cudaGetDriverEntryPoint(cuCtxGetCurrent): %s",
+                  cudaGetErrorString(e));
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+  }
+  *ctx = nullptr;
+  if (g_ctx_get_current(ctx) != CUDA_SUCCESS)
+    return fail(BPD_ERR_CUDA, "cuCtxGetCurrent failed");
+  return BPD_OK;
+}
 
 // Device address of g_noalloc_scratch on the current device. In host code the
 // symbol itself is only a host-side stand-in, so the address is looked up
-// once per device (cudaGetSymbolAddress, with that device current) and cached.
+// with cudaGetSymbolAddress (with that device current) on the first call on a
+// device and cached with the context it belongs to. A later call from another
+// context on that device (after cudaDeviceReset, say, which unloads the
+// library's module with the old context) looks the address up again.
 bpd_status noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -1001,12 +1029,18 @@ bpd_status noalloc_scratch(void** out) {
     return fail(BPD_ERR_CAPACITY, "bpd_pda_apply_mask_noalloc: device %d beyond %d", dev,
                 kMaxDevices);
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  CUcontext ctx = nullptr;
+  bpd_status rc = current_context(&ctx);
+  if (rc) return rc;
+  if (g_noalloc_ptr[dev] == nullptr || ctx == nullptr || ctx != g_noalloc_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(BPD_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    rc = current_context(&ctx);  // the lookup made the device's context current
+    if (rc) return rc;
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return BPD_OK;

@@ -128,6 +128,26 @@ def row_patterns(batch: int, seed: int = 0, n_patterns: int = len(DENSE_PATTERNS
     return [rng.randrange(n_patterns) for _ in range(batch)]
 
 
+# Global row blocks of the serving-scale dense configuration. The request
+# rows of a multi-GPU run are numbered globally and cut into blocks of
+# ROW_BLOCK rows; everything random about a row (its pattern, its logits at
+# every step) is a function of its block and its position in the block only,
+# so a rank that owns block b computes exactly what one process running the
+# whole global batch computes for those rows.
+ROW_BLOCK = 1024
+
+
+def block_patterns(block: int, rows: int = ROW_BLOCK) -> list[int]:
+    """Pattern index of each row of global row block ``block``."""
+    return row_patterns(rows, seed=block)
+
+
+def block_logits_seed(block: int, step: int) -> int:
+    """Seed of the logits of global row block ``block`` at generation step
+    ``step`` (a torch.Generator on the row block's device)."""
+    return block * 1_000_003 + step
+
+
 @dataclass(frozen=True)
 class DenseConfig:
     name: str

@@ -347,7 +347,9 @@ bpd_status bpd_pda_advance(
  * be NULL (no mask caching). Nothing here calls cudaMalloc or cudaFree.
  * The first call on a device looks up the array's device address (once per
  * device, with that device current); make that first call before any stream
- * capture. All calls share the one array, so calls that can overlap on the
+ * capture. The address is kept with the driver context it belongs to: after
+ * cudaDeviceReset the next call looks it up again in the new context (so that
+ * call, too, should come before any capture). All calls share the one array, so calls that can overlap on the
  * GPU (different streams, different host threads) race on it: serialise them
  * on one stream. Each call clears what it needs zeroed itself. */
 #define BPD_NOALLOC_MAX_BATCH 128

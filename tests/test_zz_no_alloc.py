@@ -24,6 +24,7 @@ from conftest import golden_npz
 pytestmark = pytest.mark.gpu
 
 MAX_BATCH = 128  # BPD_NOALLOC_MAX_BATCH
+MAX_VOCAB = 262144  # BPD_NOALLOC_MAX_VOCAB
 CAPACITY_ERROR = 3  # BPD_ERR_CAPACITY
 
 
@@ -97,3 +98,30 @@ def test_noalloc_rejects_batches_beyond_its_scratch() -> None:
     assert b"at most 128 rows" in L.bpd_last_error()
     torch.cuda.synchronize()
     assert (logits == 0).all()  # nothing was enqueued
+
+
+def test_noalloc_rejects_vocabularies_beyond_its_scratch() -> None:
+    """A grammar whose vocabulary is one token past the built-in limit is
+    refused before anything is enqueued (the logits stay untouched)."""
+    from bpdecode_b200 import _capi
+
+    L = _capi.lib()
+    g = _grammar("xy")
+    n = 4
+    pool = g.init_batch(n)
+    slots = torch.arange(n, device="cuda")
+    broken = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    logits = torch.zeros(n, g.vocab_size, device="cuda")
+    big = _capi.PdaGrammar.from_buffer_copy(g._struct())
+    big.vocab_size = MAX_VOCAB + 1
+    rc = L.bpd_pda_apply_mask_noalloc(
+        C.byref(big), logits.data_ptr(), 0, logits.stride(0), pool.data_ptr(),
+        slots.data_ptr(), broken.data_ptr(), n, None, 0, float("-inf"),
+        torch.cuda.current_stream().cuda_stream)
+    assert rc == CAPACITY_ERROR
+    assert b"262145" in L.bpd_last_error()
+    torch.cuda.synchronize()
+    assert (logits == 0).all()  # nothing was enqueued
+    # the same call at the real vocabulary size still works afterwards
+    assert _noalloc(L, g, logits, pool, slots, broken) == 0, L.bpd_last_error()
+    torch.cuda.synchronize()
