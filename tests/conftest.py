@@ -79,3 +79,27 @@ def vocab_of(vname: str):
 
     toks, eos = VOCABS[vname]
     return Vocabulary.from_tokens(toks, eos_id=eos)
+
+
+def reference_src() -> str | None:
+    """bpdecode's ``src/`` directory when its source tree is on this machine
+    (BPDECODE_REFERENCE, else a checkout named ``reference`` beside this
+    repository), for the tests that compare against its Python front-end;
+    None elsewhere (those tests skip)."""
+    for root in (os.environ.get("BPDECODE_REFERENCE"),
+                 os.path.join(os.path.dirname(ROOT), "reference")):
+        if root and os.path.isfile(os.path.join(root, "src", "bpdecode", "__init__.py")):
+            return os.path.join(root, "src")
+    return None
+
+
+def import_reference():
+    """Import bpdecode from its source tree (skips the test when absent)."""
+    src = reference_src()
+    if src is None:
+        pytest.skip("bpdecode's source tree is not on this machine")
+    if src not in sys.path:
+        sys.path.append(src)
+    import bpdecode  # noqa: F401
+
+    return bpdecode
