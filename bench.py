@@ -411,6 +411,24 @@ def run_profile_case(args: argparse.Namespace) -> None:
         batch.reset_many(ids)  # the captured steps start an episode, as in the bench
         for i in range(args.steps):
             step(i)
+    elif args.profile_case == "pda_misses":
+        from bpdecode_b200 import tables
+        from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
+        from bpdecode_b200.workloads import vocab_large
+
+        g = PdaTensors.from_arrays(tables.load_pda("schema"), vocab_large(V), device)
+        batch = CFGConstraintBatch(g, capacity=256)
+        ids = list(range(256))
+        for i in ids:
+            batch.add(i)
+        src = [torch.randn(256, V, device=device,
+                           generator=torch.Generator(device=device).manual_seed(500 + i))
+               for i in range(4)]
+        work = torch.empty_like(src[0])
+        g.clear_memo()
+        for i in range(n):
+            work.copy_(src[i % 4])
+            batch.step_greedy(ids, work)
     else:
         from bpdecode_b200 import tables
         from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
@@ -451,7 +469,9 @@ def main() -> None:
     ap.add_argument("--workload", default="config2", choices=["config2", "config5"],
                     help="config2 (default, the headline line) or config5 (whole-box continuous "
                          "batching: regex + schema + GBNF rows, soft lookahead, 10%% turnover)")
-    ap.add_argument("--profile-case", choices=["dense", "pda", "soft"],
+    ap.add_argument("--leg", choices=["pda_misses", "pda_config4"],
+                    help="run one side measurement alone on cuda:0 and print it")
+    ap.add_argument("--profile-case", choices=["dense", "pda", "soft", "pda_misses"],
                     help="run a few untimed steps of one hot kernel for an ncu capture "
                          "(1 GPU, --warmup steps then --steps steps) and exit")
     args = ap.parse_args()
@@ -459,6 +479,12 @@ def main() -> None:
         ap.error("--warmup must be >= 3")
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.leg:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        fn = {"pda_misses": _pda_misses, "pda_config4": _pda_config4}[args.leg]
+        print(json.dumps({args.leg: fn(dev, 0)}), flush=True)
         return
     if args.workload == "config5" and args.impl == "ours":
         run_config5(args)
@@ -626,6 +652,7 @@ def main() -> None:
         del bufs
         torch.cuda.empty_cache()
         line["pda_config4"] = _pda_config4(device, rank)
+        line["pda_misses"] = _pda_misses(device, rank)
         line["dense_config3"] = _dense_config3(device, rank)
         line["soft_lookahead"] = _soft_lookahead(fsas, pats, device, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -714,6 +741,24 @@ def _pda_config4(device: torch.device, rank: int, steps: int = 512) -> dict:
     torch.cuda.synchronize()
     us = sorted(_step_events(steps, fresh, lambda i: graphs[i % ring].replay()))
     del graphs
+    # where an eager step's time goes: the unfused sequence on the same rows
+    # (mask pipeline + apply, torch argmax, commit = advance_kernel), each
+    # timed alone after warm steps (every row hits the memo by then)
+    n = 32
+    part = {"apply_mask": [], "argmax": [], "commit": []}
+    for i in range(n):
+        fresh(i)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
+        batch.apply_mask(ids, bufs[i % ring])
+        ev[1].record()
+        tok = bufs[i % ring].argmax(-1)
+        ev[2].record()
+        batch.commit(ids, tok)
+        ev[3].record()
+        torch.cuda.synchronize()
+        for k, name in enumerate(part):
+            part[name].append(ev[k].elapsed_time(ev[k + 1]) * 1000)
     broken = int(batch._broken.sum())
     return {"workload": "recursive JSON-value GBNF, PDA, 256 rows, V=128256, fp32 N(0,1) "
                         f"+3 bias, memo cleared at start, {steps} steps, unmasked logits "
@@ -722,9 +767,88 @@ def _pda_config4(device: torch.device, rank: int, steps: int = 512) -> dict:
             "graph_step_us_median": us[len(us) // 2], "graph_step_us_p90": us[int(len(us) * 0.9)],
             "eager_step_us_median": sorted(eager)[len(eager) // 2],
             "first_step_us_cold_memo": first,
+            "unfused_us_median": {k: sorted(v)[len(v) // 2] for k, v in part.items()},
             "row_steps_per_s": B / (us[len(us) // 2] * 1e-6), "broken_rows_at_end": broken,
             "note": "the bounded PDA saturates at init on this grammar (8 configs), as the "
                     "reference does; after the first steps every row's config-set hits the memo"}
+
+
+def _canon_rows(cfg) -> list[bytes]:
+    """The live content of each 266-int config row (num_configs, depths and
+    frames of the live configs), as bytes: equal content, equal mask."""
+    import numpy as np
+
+    out = []
+    for r in cfg:
+        n = int(r[0])
+        d = r[2:2 + n]
+        parts = [np.int32(n).tobytes(), d.tobytes()]
+        parts += [r[10 + 32 * i:10 + 32 * i + int(d[i])].tobytes() for i in range(n)]
+        out.append(b"".join(parts))
+    return out
+
+
+def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2) -> dict:
+    """The PDA path on a grammar that keeps producing config-sets the memo
+    has not seen: the JSON-Schema object of config 3 as a PDA (its 1354-state
+    rule NFAs, not the dense DFA), 256 rows, V = 128,256, fp32 N(0, 1), greedy;
+    the memo and the transition cache are cleared at the start of each
+    32-step generation. Per step: device time (CUDA events around
+    CFGConstraintBatch.step_greedy, issued eagerly) and the number of distinct
+    config-sets the rows hold that the generation had not seen before (read
+    between steps, untimed)."""
+    from bpdecode_b200 import tables
+    from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
+    from bpdecode_b200.workloads import vocab_large
+
+    B = 256
+    g = PdaTensors.from_arrays(tables.load_pda("schema"), vocab_large(V), device)
+    batch = CFGConstraintBatch(g, capacity=B)
+    ids = list(range(B))
+    for i in ids:
+        batch.add(i)
+    ring = 16
+    src = [torch.randn(B, V, device=device,
+                       generator=torch.Generator(device=device).manual_seed(rank * 97 + 500 + i))
+           for i in range(ring)]
+    work = torch.empty_like(src[0])
+    for i in range(2):  # load the kernels, allocate the memo and workspace
+        work.copy_(src[i])
+        batch.step_greedy(ids, work)
+    us: list[list[float]] = []
+    new: list[list[int]] = []
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    for gen in range(gens):
+        g.clear_memo()
+        for r in ids:
+            batch.reset(r)
+        seen: set[bytes] = set()
+        us.append([])
+        new.append([])
+        for step in range(steps):
+            rows = set(_canon_rows(batch._configs.cpu().numpy()))
+            new[-1].append(len(rows - seen))
+            seen |= rows
+            work.copy_(src[(gen * steps + step) % ring])
+            torch.cuda.synchronize()
+            a.record()
+            batch.step_greedy(ids, work)
+            b.record()
+            torch.cuda.synchronize()
+            us[-1].append(a.elapsed_time(b) * 1000)
+    flat = [x for u in us for x in u]
+    miss = [x for u, n in zip(us, new) for x, k in zip(u, n) if k > 0]
+    return {"workload": "JSON-Schema object as a PDA (1354 states), 256 rows, V=128256, fp32 "
+                        f"N(0,1), greedy, {gens} generations of {steps} steps, memo and "
+                        "transition cache cleared at the start of each",
+            "step": "CFGConstraintBatch.step_greedy, eager",
+            "us_per_step_mean": statistics.fmean(flat),
+            "us_per_step_with_new_sets_mean": statistics.fmean(miss) if miss else None,
+            "steps_with_new_sets": len(miss), "steps": len(flat),
+            "us_first_step": [u[0] for u in us],
+            "new_sets_per_step": new[0],
+            "us_per_step": [round(x, 1) for x in us[0]]}
 
 
 def _dense_config3(device: torch.device, rank: int, steps: int = 256) -> dict:

@@ -198,6 +198,22 @@ __device__ __forceinline__ void w_copy(int32_t* dst, const int32_t* src, int lan
 // ---------------------------------------------------------------------------
 // Memo / workspace layout.
 
+// Transition cache of the miss path: config-sets that token walks reach,
+// interned as nodes (canonical content, as memo keys), each with its 256
+// byte transitions filled in as walks need them. It turns the walks through
+// regular stretches of a grammar (string bodies, numbers, keywords -- the
+// regular sub-loops) into table walks, like a DFA's tok_next, while every
+// transition is still the bounded closure of the reference on the node's
+// exact content.
+struct Nodes {
+  unsigned long long* hash;  // [ncap] 0 = free, else (content hash | 1): slot claimed
+  uint32_t* ready;           // [ncap] 1 once the slot's key is written
+  int32_t* key;              // [ncap][NCFG] canonical config-sets
+  int32_t* trans;            // [ncap][256] 0 unknown, 1 being computed, 2 the set dies,
+                             //             3 + id: next node
+  int32_t cap;               // power of two, 0 = none
+};
+
 struct Memo {
   uint32_t* epoch;  // [1] calls so far; entries claimed by the running call carry
                     //     tag epoch + 1 and are skipped by its own lookups
@@ -207,7 +223,13 @@ struct Memo {
   uint32_t* bits;   // [cap][ws] allow rows
   int32_t cap;      // power of two, 0 = no memo
   int32_t ws;       // words per allow row (multiple of 4)
+  Nodes nodes;      // transition cache (kNodesPerEntry per memo entry)
 };
+
+constexpr int32_t kNodesPerEntry = 4;
+#ifndef BPD_PDA_NODES
+#define BPD_PDA_NODES 1  // 0: miss path without the transition cache (for comparisons)
+#endif
 
 
 constexpr int32_t words_stride(int32_t vocab) { return ((((vocab + 31) / 32) + 3) / 4) * 4; }
@@ -227,13 +249,33 @@ Memo memo_view(void* base, int32_t cap, int32_t vocab) {
   m.key = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * NCFG * static_cast<size_t>(cap));
   m.bits = reinterpret_cast<uint32_t*>(p);
+  p += align256(sizeof(uint32_t) * m.ws * static_cast<size_t>(cap));
+  const size_t ncap = static_cast<size_t>(cap) * kNodesPerEntry;
+  m.nodes.cap = static_cast<int32_t>(ncap);
+  m.nodes.hash = reinterpret_cast<unsigned long long*>(p);
+  p += align256(sizeof(unsigned long long) * ncap);
+  m.nodes.ready = reinterpret_cast<uint32_t*>(p);
+  p += align256(sizeof(uint32_t) * ncap);
+  m.nodes.trans = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * 256 * ncap);
+  m.nodes.key = reinterpret_cast<int32_t*>(p);
   return m;
 }
 
+// Bytes of the node table's parts that a reset zeroes (hash, ready, trans),
+// counted from nodes.hash.
+size_t nodes_clear_bytes(int32_t cap) {
+  const size_t ncap = static_cast<size_t>(cap) * kNodesPerEntry;
+  return align256(sizeof(unsigned long long) * ncap) + align256(sizeof(uint32_t) * ncap) +
+         align256(sizeof(int32_t) * 256 * ncap);
+}
+
 size_t memo_bytes(int32_t cap, int32_t vocab) {
+  const size_t ncap = static_cast<size_t>(cap) * kNodesPerEntry;
   return 256 + align256(sizeof(uint32_t) * cap) + align256(sizeof(uint64_t) * cap) +
          align256(sizeof(int32_t) * NCFG * static_cast<size_t>(cap)) +
-         align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(cap));
+         align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(cap)) +
+         nodes_clear_bytes(cap) + align256(sizeof(int32_t) * NCFG * ncap);
 }
 
 // Row kinds (Work::kind).
@@ -252,6 +294,7 @@ struct Work {
   uint64_t* hash;    // [batch]
   uint32_t* first;   // [batch][8] surviving first bytes (representatives)
   int32_t* eos_ok;   // [batch]
+  int32_t* node;     // [batch] node of a representative's config-set (-1: none)
   uint32_t* bits;    // [batch][ws] allow rows of representatives without a memo entry
 };
 
@@ -283,6 +326,8 @@ Work work_view(void* base, int32_t batch, int32_t vocab) {
   p += align256(sizeof(uint32_t) * 8 * batch);
   w.eos_ok = reinterpret_cast<int32_t*>(p);
   p += align256(sizeof(int32_t) * batch);
+  w.node = reinterpret_cast<int32_t*>(p);
+  p += align256(sizeof(int32_t) * batch);
   w.bits = reinterpret_cast<uint32_t*>(p);
   return w;
 }
@@ -292,7 +337,7 @@ constexpr size_t work_bytes(int32_t batch, int32_t vocab) {
   return align256(sizeof(int32_t) * (dcap + 4)) + step_scratch_bytes(batch) +
          3 * align256(sizeof(int32_t) * batch) +
          align256(sizeof(uint64_t) * batch) + align256(sizeof(uint32_t) * 8 * batch) +
-         align256(sizeof(int32_t) * batch) +
+         2 * align256(sizeof(int32_t) * batch) +
          align256(sizeof(uint32_t) * words_stride(vocab) * static_cast<size_t>(batch));
 }
 
@@ -369,6 +414,119 @@ __device__ __forceinline__ bool w_same_words(const int32_t* a, const int32_t (&k
 
 __device__ __forceinline__ int64_t slot_of(const int64_t* slots, int32_t b) {
   return slots ? slots[b] : b;
+}
+
+// ---------------------------------------------------------------------------
+// Transition cache (see Nodes). Waits are bounded: a warp that finds a slot
+// or a transition another warp is filling polls it at most kNodePolls times
+// (the filler is a running warp that waits on nothing itself) and then goes
+// on without it -- a duplicate node or a recomputed transition, never a
+// different result.
+
+constexpr int kNodeProbe = 64;
+constexpr int kNodePolls = 1 << 14;
+constexpr int32_t kTransUnknown = 0, kTransBusy = 1, kTransDead = 2, kTransNode = 3;
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int32_t ld_acquire_s32(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Node of config-set `c` (shared memory; any words outside its live region)
+// with content hash `h`: found, or claimed and written here; -1 when the
+// probe sequence is full.
+__device__ int32_t node_intern(const Nodes& nd, const int32_t* c, uint64_t h, int lane) {
+  const unsigned long long hv = static_cast<unsigned long long>(h) | 1ull;
+  for (int p = 0; p < kNodeProbe; ++p) {
+    const int32_t e = static_cast<int32_t>((h + static_cast<uint64_t>(p)) &
+                                           static_cast<uint64_t>(nd.cap - 1));
+    unsigned long long cur = 0;
+    if (lane == 0) {
+      cur = atomicAdd(nd.hash + e, 0ull);
+      if (cur == 0ull) cur = atomicCAS(nd.hash + e, 0ull, hv);
+    }
+    cur = __shfl_sync(kAll, cur, 0);
+    if (cur == 0ull) {  // this warp claimed the slot: write the key, then publish it
+      int32_t* key = nd.key + static_cast<int64_t>(e) * NCFG;
+      for (int k = lane; k < NCFG; k += 32) key[k] = canon_word(c, k);
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) atomicExch(nd.ready + e, 1u);
+      return e;
+    }
+    if (cur != hv) continue;
+    uint32_t rdy = 0;
+    if (lane == 0) {
+      rdy = ld_acquire_u32(nd.ready + e);
+      for (int i = 0; rdy == 0u && i < kNodePolls; ++i) {
+        __nanosleep(64);
+        rdy = ld_acquire_u32(nd.ready + e);
+      }
+    }
+    rdy = __shfl_sync(kAll, rdy, 0);
+    if (rdy == 0u) continue;  // not written in time: look further (a duplicate at worst)
+    __syncwarp();
+    const int32_t* key = nd.key + static_cast<int64_t>(e) * NCFG;
+    int32_t kw[kRowWords];
+#pragma unroll
+    for (int j = 0; j < kRowWords; ++j) {
+      const int k = lane + 32 * j;
+      kw[j] = k < NCFG ? __ldcg(key + k) : 0;
+    }
+    if (w_same_words(c, kw, lane)) return e;
+  }
+  return -1;
+}
+
+// The node after byte `byte` from node q: >= 0 a node, -1 the set dies, -2
+// the next set could not be interned (table full) -- then `next` holds it.
+// `cur` and `next` are NCFG words of this warp's shared memory. A known
+// transition is read from the table; an unknown one is computed here (the
+// bounded closure, w_advance_byte, on q's content) and stored.
+__device__ int32_t node_step(const bpd_pda_grammar& g, const Nodes& nd, int32_t q, int byte,
+                             int32_t* cur, int32_t* next, int lane) {
+  if (q < 0 || q >= nd.cap) return -2;  // not a node: callers never pass one
+  int32_t* slot = nd.trans + static_cast<int64_t>(q) * 256 + byte;
+  int32_t v = 0;
+  bool own = false;
+  if (lane == 0) {
+    v = ld_acquire_s32(slot);
+    if (v == kTransUnknown) {
+      v = atomicCAS(slot, kTransUnknown, kTransBusy);
+      own = v == kTransUnknown;
+    }
+    for (int i = 0; v == kTransBusy && !own && i < kNodePolls; ++i) {
+      __nanosleep(64);
+      v = ld_acquire_s32(slot);
+    }
+  }
+  own = __shfl_sync(kAll, own, 0);
+  v = __shfl_sync(kAll, v, 0);
+  if (!own && v == kTransDead) return -1;
+  if (!own && v >= kTransNode && v - kTransNode < nd.cap) return v - kTransNode;
+  // compute it (owner, or after a wait that ran out: then without storing);
+  // q came from a transition another warp may have stored just now: order
+  // the key's reads after it
+  __threadfence();
+  const int32_t* key = nd.key + static_cast<int64_t>(q) * NCFG;
+  for (int k = lane; k < NCFG; k += 32) cur[k] = __ldcg(key + k);
+  __syncwarp();
+  int32_t r = -1;
+  if (w_advance_byte<false>(g, cur, next, byte, lane)) {
+    const int32_t e = node_intern(nd, next, w_hash(next, lane), lane);
+    r = e >= 0 ? e : -2;
+  }
+  if (own && lane == 0) {
+    __threadfence();
+    atomicExch(slot, r == -1 ? kTransDead : r >= 0 ? kTransNode + r : kTransUnknown);
+  }
+  return r;
 }
 
 // ---------------------------------------------------------------------------
@@ -472,6 +630,12 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
       }
     }
   }
+  if (kind == kRep) {
+    // the representative's node: its walks start there
+    const int32_t nd = (BPD_PDA_NODES && memo.nodes.cap) ? node_intern(memo.nodes, A, h, lane)
+                                                         : -1;
+    if (lane == 0) w.node[b] = nd;
+  }
   if (lane == 0) {
     w.kind[b] = kind;
     w.ref[b] = ref;
@@ -509,6 +673,70 @@ __device__ __forceinline__ uint32_t* rep_bits(const Memo& memo, const Work& w, i
   return w.bits + static_cast<int64_t>(b) * memo.ws;
 }
 
+// Token walks of a warp through the transition cache, lane = token: a lane
+// with `walk` set follows its token's bytes from node nd0, from the first
+// byte on. Transitions the table does not hold yet are computed by the
+// whole warp, one at a time (node_step; another warp computing the same one
+// is waited for, boundedly); a lane whose next set cannot be interned
+// finishes its token with direct byte steps from that set. Sets `ok` of
+// every lane with `walk`.
+__device__ __forceinline__ void node_walk(const bpd_pda_grammar& g, const Nodes& nd, int32_t nd0,
+                                          int32_t o0, int32_t o1, bool walk, bool& ok,
+                                          int32_t (*buf)[NCFG], int lane) {
+  bool active = walk;
+  int32_t q = nd0, i = o0;
+  for (;;) {
+    int32_t byte = 0;
+    while (active) {
+      if (i == o1) {
+        ok = true;
+        active = false;
+        break;
+      }
+      byte = __ldg(g.tok_bytes + i);
+      const int32_t v = __ldcg(nd.trans + static_cast<int64_t>(q) * 256 + byte);
+      if (v >= kTransNode && v - kTransNode < nd.cap) {
+        q = v - kTransNode;
+        ++i;
+      } else if (v == kTransDead) {
+        ok = false;
+        active = false;
+      } else {
+        break;  // unknown, or being computed: the warp takes it below
+      }
+    }
+    const uint32_t need = __ballot_sync(kAll, active);
+    if (need == 0u) break;
+    const int j = __ffs(need) - 1;
+    const int32_t qj = __shfl_sync(kAll, q, j);
+    const int32_t bj = __shfl_sync(kAll, byte, j);
+    const int32_t r = node_step(g, nd, qj, bj, buf[0], buf[1], lane);
+    if (r == -2) {
+      // not interned: the rest of lane j's token by direct byte steps
+      const int32_t k0 = __shfl_sync(kAll, i, j) + 1, k1 = __shfl_sync(kAll, o1, j);
+      const int32_t* c = buf[1];
+      bool alive = true;
+      for (int32_t k = k0; k < k1 && alive; ++k) {
+        int32_t* n = c == buf[1] ? buf[0] : buf[1];
+        alive = w_advance_byte<false>(g, c, n, __ldg(g.tok_bytes + k), lane);
+        c = n;
+      }
+      if (lane == j) {
+        ok = alive;
+        active = false;
+      }
+    } else if (lane == j) {
+      if (r == -1) {
+        ok = false;
+        active = false;
+      } else {
+        q = r;
+        ++i;
+      }
+    }
+  }
+}
+
 constexpr int32_t kComputeChunk = kWarps * 32 * 4;  // tokens per compute item
 
 // Allow bits of every representative row. Items are (representative, 1024
@@ -519,8 +747,8 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
                                               const int32_t* __restrict__ pool,
                                               const int64_t* __restrict__ slots,
                                               const Memo& memo, const Work& w,
-                                              int32_t (*buf)[2][NCFG], uint32_t* first,
-                                              int32_t& s_item) {
+                                              bool first_valid, int32_t (*buf)[2][NCFG],
+                                              uint32_t* first, int32_t& s_item) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int32_t V = g.vocab_size;
   const int32_t chunks = (V + kComputeChunk - 1) / kComputeChunk;
@@ -536,10 +764,12 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
     const int32_t c0 = (item % chunks) * kComputeChunk;
     const int32_t c1 = min(V, c0 + kComputeChunk);
     const int32_t* base = pool + slot_of(slots, b) * NCFG;
-    if (threadIdx.x < 8) first[threadIdx.x] = w.first[static_cast<int64_t>(b) * 8 + threadIdx.x];
+    if (first_valid && threadIdx.x < 8)
+      first[threadIdx.x] = w.first[static_cast<int64_t>(b) * 8 + threadIdx.x];
     __syncthreads();
     const bool eos_ok = w.eos_ok[b] != 0;
     const bool nonempty = n_of(base) > 0;
+    const int32_t nd0 = w.node[b];
     uint32_t* out = rep_bits(memo, w, b);
     for (int32_t t0 = c0 + warp * 32; t0 < c1; t0 += kWarps * 32) {
       const int32_t t = t0 + lane;
@@ -553,6 +783,8 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
           o1 = __ldg(g.tok_offsets + t + 1);
           if (o0 == o1) {
             ok = nonempty;
+          } else if (nd0 >= 0 || !first_valid) {
+            walk = true;  // through the transition cache, or a direct walk
           } else {
             const int fb = __ldg(g.tok_bytes + o0);
             if ((first[fb >> 5] >> (fb & 31)) & 1u) {
@@ -561,6 +793,10 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
             }
           }
         }
+      }
+      if (nd0 >= 0) {
+        node_walk(g, memo.nodes, nd0, o0, o1, walk, ok, buf[warp], lane);
+        walk = false;
       }
       uint32_t todo = __ballot_sync(kAll, walk);
       while (todo) {
@@ -610,11 +846,11 @@ __global__ void __launch_bounds__(kThreads)
 
 __global__ void __launch_bounds__(kThreads)
     compute_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
-                   const int64_t* __restrict__ slots, Memo memo, Work w) {
+                   const int64_t* __restrict__ slots, Memo memo, Work w, int32_t first_valid) {
   __shared__ int32_t buf[kWarps][2][NCFG];
   __shared__ uint32_t first[8];
   __shared__ int32_t s_item;
-  compute_items(g, pool, slots, memo, w, buf, first, s_item);
+  compute_items(g, pool, slots, memo, w, first_valid != 0, buf, first, s_item);
   // the last kernel of every mask call: the next call gets a new tag (the
   // lookups of this call, which read the old epoch, have all finished)
   if (memo.cap && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -785,10 +1021,17 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
   rc = check_launch("pda lookup_kernel");
   if (rc) return rc;
   const int32_t sms = sm_count();
-  first_byte_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, w);
-  rc = check_launch("pda first_byte_kernel");
-  if (rc) return rc;
-  compute_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, memo, w);
+  // With a transition cache the compute walks take every token from its
+  // first byte through the cache; without one, the first bytes that keep
+  // each representative alive are found first, so that tokens starting with
+  // any other byte are rejected without a walk.
+  const bool nodes = BPD_PDA_NODES && memo.nodes.cap > 0;
+  if (!nodes) {
+    first_byte_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, w);
+    rc = check_launch("pda first_byte_kernel");
+    if (rc) return rc;
+  }
+  compute_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, memo, w, nodes ? 0 : 1);
   rc = check_launch("pda compute_kernel");
   if (rc) return rc;
   *memo_out = memo;
@@ -837,8 +1080,10 @@ extern "C" bpd_status bpd_pda_memo_reset(void* memo, int32_t capacity, int32_t v
               "bpd_pda_memo_reset: capacity must be a power of two");
   BPD_REQUIRE(vocab_size > 0, "bpd_pda_memo_reset: bad vocab");
   Memo m = memo_view(memo, capacity, vocab_size);
-  const cudaError_t e = cudaMemsetAsync(m.epoch, 0, 256 + sizeof(uint32_t) * capacity,
-                                        as_stream(stream));
+  cudaError_t e = cudaMemsetAsync(m.epoch, 0, 256 + sizeof(uint32_t) * capacity,
+                                  as_stream(stream));
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memo reset: %s", cudaGetErrorString(e));
+  e = cudaMemsetAsync(m.nodes.hash, 0, nodes_clear_bytes(capacity), as_stream(stream));
   if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memo reset: %s", cudaGetErrorString(e));
   return BPD_OK;
 }

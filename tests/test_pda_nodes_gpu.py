@@ -1,0 +1,132 @@
+"""The PDA miss path with its transition cache, on workloads that keep
+missing the mask memo, against the reference's own CUDA build.
+
+Every config-set a token walk reaches is interned as a node with 256 byte
+transitions filled in on demand, so repeated walks through the same stretch
+of a grammar become table walks. Each transition is the bounded closure on
+the node's exact content, so masks, tokens and full 266-int config rows must
+stay bit-identical to the reference's apply_mask_pda / advance_state_pda
+kernels (pda_cuda.cu:72-117). The node table lives in the grammar's memo
+buffer; a memo of capacity c holds 4c nodes, so tiny capacities force the
+fallbacks (a next set that cannot be interned, a first transition that is not
+cached) on every step.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle.oracle import RefCudaLib
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not RefCudaLib.available(),
+                       reason="the reference's CUDA sources were not compiled (oracle/_ref)"),
+]
+
+
+def _grammar(name: str, V: int, memo_capacity: int):
+    from bpdecode_b200 import tables
+    from bpdecode_b200.grammar import device
+    from bpdecode_b200.workloads import vocab_large
+
+    g = device.PdaTensors.from_arrays(tables.load_pda(name), vocab_large(V), "cuda")
+    old = device.DEFAULT_MEMO_CAPACITY
+    device.DEFAULT_MEMO_CAPACITY = memo_capacity
+    try:
+        g.mask_memo()  # allocated (and cleared) at this capacity
+    finally:
+        device.DEFAULT_MEMO_CAPACITY = old
+    return g
+
+
+def _run_against_reference(name: str, V: int, B: int, steps: int, memo_capacity: int,
+                           seed: int, bias: float = 0.0) -> int:
+    """Greedy generation of B rows on fresh logits every step; returns how
+    many distinct config-sets the rows went through."""
+    from bpdecode_b200.grammar.device import CFGConstraintBatch
+    from bpdecode_b200.workloads import BIASED, vocab_large
+
+    ref = RefCudaLib()
+    g = _grammar(name, V, memo_capacity)
+    batch = CFGConstraintBatch(g, capacity=B)
+    ids = list(range(B))
+    for i in ids:
+        batch.add(i)
+    ref_cfg = batch._configs.clone()
+    vocab = vocab_large(V)
+    boost = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    seen: set[bytes] = set()
+    ref_broken = torch.zeros(B, dtype=torch.bool, device="cuda")
+    for step in range(steps):
+        for row in batch._configs.cpu().numpy():
+            seen.add(row.tobytes())
+        logits = torch.randn(B, V, generator=gen, device="cuda")
+        if bias:
+            logits[:, boost] += bias
+        mine, want = logits.clone(), logits.clone()
+        tok = batch.step_greedy(ids, mine)
+        # the reference's CFGConstraintBatch step (grammar/device.py:252-283)
+        ref.pda_apply_mask(g, ref_cfg, want)
+        want[ref_broken] = float("-inf")
+        ref_tok = want.argmax(-1)
+        ok = ref.pda_advance(g, ref_cfg, ref_tok.to(torch.int32))
+        ref_broken |= ok == 0
+        assert torch.equal(mine, want), (name, step)
+        assert torch.equal(tok, ref_tok), (name, step)
+        assert torch.equal(batch._configs, ref_cfg), (name, step)
+        assert torch.equal(batch._broken.bool(), ref_broken), (name, step)
+    return len(seen)
+
+
+@pytest.mark.parametrize("memo_capacity", [4096, 16, 1])
+@pytest.mark.parametrize("name", ["schema", "jsonvalue", "pairs", "paren", "hf_object"])
+def test_generation_equals_reference_cuda(name: str, memo_capacity: int) -> None:
+    distinct = _run_against_reference(name, 4096, 96, 24, memo_capacity, seed=5,
+                                      bias=2.0 if name in ("paren", "jsonvalue") else 0.0)
+    assert distinct > 1
+
+
+def test_schema_misses_at_full_vocabulary_equal_reference_cuda() -> None:
+    """The miss workload of the benchmark's PDA leg: the JSON-Schema object
+    as a PDA, 256 rows, V = 128,256, fp32 N(0, 1), greedy, memo cleared at the
+    start; most steps bring config-sets the memo has not seen."""
+    distinct = _run_against_reference("schema", 128_256, 256, 24, 4096, seed=9)
+    assert distinct > 24
+
+
+def test_paren_nesting_walks_equal_reference_cuda() -> None:
+    """paren = "(" paren ")" | "x" | "y" with "(" favoured: the stack deepens
+    every step (a new config-set each step) up to the 32-frame cap, where the
+    bounded PDA saturates."""
+    from bpdecode_b200.grammar.device import CFGConstraintBatch
+
+    ref = RefCudaLib()
+    V = 8192
+    g = _grammar("paren", V, 4096)
+    from bpdecode_b200.workloads import vocab_large
+
+    vocab = vocab_large(V)
+    opens = torch.tensor([i for i, t in enumerate(vocab.token_bytes)
+                          if t and set(t) <= {ord("(")}], device="cuda")
+    assert len(opens) > 0
+    B = 32
+    batch = CFGConstraintBatch(g, capacity=B)
+    ids = list(range(B))
+    for i in ids:
+        batch.add(i)
+    ref_cfg = batch._configs.clone()
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    for step in range(40):
+        logits = torch.randn(B, V, generator=gen, device="cuda")
+        logits[:, opens] += 6.0
+        mine, want = logits.clone(), logits.clone()
+        tok = batch.step_greedy(ids, mine)
+        ref.pda_apply_mask(g, ref_cfg, want)
+        ref_tok = want.argmax(-1)
+        ref.pda_advance(g, ref_cfg, ref_tok.to(torch.int32))
+        assert torch.equal(mine, want), step
+        assert torch.equal(tok, ref_tok), step
+        assert torch.equal(batch._configs, ref_cfg), step
