@@ -61,12 +61,18 @@ __device__ __forceinline__ const int32_t* st_of(const int32_t* c, int i) {
   return c + 2 + MC + i * MD;
 }
 
-// Is a config equal to the candidate (depth cd; lane k holds frame k) in `c`?
-// pda.hpp:102-108.
+// Is a config equal to the candidate (depth cd >= 1; lane k holds frame k)
+// in `c`? pda.hpp:102-108. Lane j < num_configs first checks config j's depth
+// and top frame against the candidate's (one ballot); only the configs that
+// pass are compared frame by frame.
 __device__ __forceinline__ bool w_contains(const int32_t* c, int cd, int32_t v, int lane) {
   const int n = n_of(c);
-  for (int j = 0; j < n; ++j) {
-    if (c[2 + j] != cd) continue;
+  const int32_t top = __shfl_sync(kAll, v, cd - 1);
+  const bool maybe = lane < n && c[2 + lane] == cd && st_of(c, lane)[cd - 1] == top;
+  uint32_t cand = __ballot_sync(kAll, maybe);
+  while (cand != 0u) {
+    const int j = __ffs(cand) - 1;
+    cand &= cand - 1u;
     const bool eq = lane >= cd || st_of(c, j)[lane] == v;
     if (__all_sync(kAll, eq)) return true;
   }

@@ -100,3 +100,68 @@ def test_regex_processor_matches_batch(soft_k) -> None:
         assert torch.equal(got, want)
         tok = got.argmax(-1)
         input_ids = torch.cat([input_ids, tok.unsqueeze(1)], dim=1)
+
+
+def _reference_processor_step(ref, hg, cfgs, broken, scores, input_ids, first: bool,
+                              neg_inf: float = float("-inf")) -> None:
+    """bpdecode's GrammarLogitsProcessor device backend (hf.py:226-259) on the
+    host, with the reference's own compiled PDA (pda_cpu.cpp): commit the last
+    token (CFGConstraintBatch.commit, grammar/device.py:268-283), then mask
+    padded columns, mask the rows (broken rows entirely) on an fp32 working
+    copy and copy it back."""
+    import numpy as np
+
+    if not first:
+        ok = ref.pda_advance(hg, cfgs, input_ids[:, -1].cpu().numpy().astype(np.int32))
+        broken |= ok == 0
+    v = hg.vocab_size
+    work = scores.float().cpu().numpy()
+    work[:, v:] = neg_inf
+    part = np.ascontiguousarray(work[:, :v])
+    ref.pda_apply_mask(hg, cfgs, part, neg_inf)
+    part[broken] = neg_inf
+    work[:, :v] = part
+    scores.copy_(torch.from_numpy(work).to(scores.device))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("name", ["hf_object", "jsonvalue", "schema"])
+def test_grammar_processor_equals_reference_processor(name: str, dtype: torch.dtype) -> None:
+    """Our processor and the reference processor's sequence on the same
+    scores every step (padded columns, fp32 and bf16), greedy tokens fed back:
+    the masked scores are identical."""
+    import numpy as np
+
+    from oracle.oracle import HostPda, RefLib
+
+    if not RefLib.available():
+        pytest.skip("the reference's CPU sources were not compiled (oracle/_ref)")
+    from bpdecode_b200 import tables
+    from bpdecode_b200.grammar.device import PdaTensors
+    from bpdecode_b200.hf import GrammarLogitsProcessor
+    from bpdecode_b200.workloads import vocab_large
+
+    ref = RefLib()
+    vocab = vocab_large(4096)
+    arrays = tables.load_pda(name)
+    lp = GrammarLogitsProcessor(PdaTensors.from_arrays(arrays, vocab), vocab, device="cuda")
+    offs = np.zeros(vocab.size + 1, np.int32)
+    np.cumsum([len(t) for t in vocab.token_bytes], out=offs[1:])
+    hg = HostPda(arrays, offs, np.frombuffer(b"".join(vocab.token_bytes), np.uint8),
+                 vocab.eos_id)
+    rows, pad = 6, 11
+    cfgs = np.stack([ref.pda_init(hg)] * rows)
+    broken = np.zeros(rows, bool)
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    input_ids = torch.zeros(rows, 1, dtype=torch.long, device="cuda")
+    for step in range(16):
+        scores = (torch.randn(rows, vocab.size + pad, generator=gen, device="cuda") * 2
+                  ).to(dtype)
+        want = scores.clone()
+        _reference_processor_step(ref, hg, cfgs, broken, want, input_ids, step == 0)
+        got = lp(input_ids, scores)
+        assert got is scores
+        assert torch.equal(got.view(torch.int16 if dtype != torch.float32 else torch.int32),
+                           want.view(torch.int16 if dtype != torch.float32 else torch.int32)), step
+        tok = got.float().argmax(-1)
+        input_ids = torch.cat([input_ids, tok.unsqueeze(1)], dim=1)
