@@ -200,7 +200,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_worker(rank: int, world: int, port: int, steps: int, out) -> None:
+def _rank_worker(rank: int, world: int, port: int, steps: int, outdir: str) -> None:
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank),
                       MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     import sys
@@ -216,11 +216,14 @@ def _rank_worker(rank: int, world: int, port: int, steps: int, out) -> None:
     block = bench.my_block(rank, world)
     tok, state = _block_run([block], steps, dev)
     shard.barrier()
-    out.put((rank, block, tok.numpy(), state.numpy()))
+    # results go to a file, not a pipe: a pipe holds 64 KB, and a writer
+    # blocked on it would never reach the exit the parent joins on
+    np.savez(os.path.join(outdir, f"rank{rank}.npz"), block=block, tok=tok.numpy(),
+             state=state.numpy())
     shard.finish()
 
 
-def test_two_ranks_reproduce_the_one_process_run() -> None:
+def test_two_ranks_reproduce_the_one_process_run(tmp_path) -> None:
     """Two processes (one GPU each where there are two, else both on cuda:0;
     no kernel of one waits on the other), gloo for the group: rank r runs its
     global row block; the gathered tokens and states equal one process over
@@ -229,13 +232,12 @@ def test_two_ranks_reproduce_the_one_process_run() -> None:
 
     bench = _bench()
     world, steps, R = 2, 8, bench.ROWS_PER_GPU
-    ctx = mp.get_context("spawn")
-    q = ctx.SimpleQueue()
-    mp.start_processes(_rank_worker, args=(world, _free_port(), steps, q), nprocs=world,
-                       join=True, start_method="spawn")
-    got = sorted((q.get() for _ in range(world)), key=lambda x: x[0])
+    mp.start_processes(_rank_worker, args=(world, _free_port(), steps, str(tmp_path)),
+                       nprocs=world, join=True, start_method="spawn")
     whole_tok, whole_state = _block_run([0, 1], steps, torch.device("cuda", 0))
-    for rank, block, tok, state in got:
+    for rank in range(world):
+        with np.load(tmp_path / f"rank{rank}.npz") as z:
+            block, tok, state = int(z["block"]), z["tok"], z["state"]
         assert block == rank
         assert np.array_equal(tok, whole_tok[:, block * R:(block + 1) * R].numpy()), rank
         assert np.array_equal(state, whole_state[block * R:(block + 1) * R].numpy()), rank
