@@ -346,16 +346,24 @@ class ConstraintBatch:
 
     # --- per-step ------------------------------------------------------
     def _slots(self, seq_ids: Sequence[Hashable]) -> torch.Tensor:
+        return self._slots_arg(seq_ids)[0]
+
+    def _slots_arg(self, seq_ids: Sequence[Hashable]) -> tuple[torch.Tensor, int | None]:
+        """The device slot tensor of ``seq_ids`` and the pointer the kernels
+        get for it: None when row b is slot b for every row (the kernels then
+        skip the slot load, one dependent load less per row)."""
         key = seq_ids if isinstance(seq_ids, tuple) else tuple(seq_ids)
         hit = self._slot_cache.get(key)
         if hit is not None:
             self._slot_cache.move_to_end(key)
             return hit
-        slots = _upload([self._slot_of[s] for s in key], torch.int64, self.device)
-        self._slot_cache[key] = slots
+        host = [self._slot_of[s] for s in key]
+        slots = _upload(host, torch.int64, self.device)
+        hit = (slots, None if all(s == i for i, s in enumerate(host)) else slots.data_ptr())
+        self._slot_cache[key] = hit
         if len(self._slot_cache) > self._SLOT_CACHE:
             self._slot_cache.popitem(last=False)
-        return slots
+        return hit
 
     def apply_mask(
         self,
@@ -365,7 +373,7 @@ class ConstraintBatch:
     ) -> torch.Tensor:
         """In place: push every grammar-disallowed logit in ``logits``
         ``[len(seq_ids), vocab]`` to ``neg_inf``, one row per ``seq_ids`` entry."""
-        slots = self._slots(seq_ids)
+        slots, slot_ptr = self._slots_arg(seq_ids)
         if self.cache is not None:
             self.cache.apply(self._state[slots], logits, neg_inf)
             return logits
@@ -377,7 +385,7 @@ class ConstraintBatch:
         L = _capi.lib()
         L.check(L.bpd_dense_apply_mask(
             logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
-            slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1], t.num_states,
+            slot_ptr, t.allow_bits.data_ptr(), t.allow_bits.shape[1], t.num_states,
             float(neg_inf), _stream(logits)))
         return logits
 
@@ -428,7 +436,7 @@ class ConstraintBatch:
         """NEW: ``apply_mask`` + ``logits.argmax(-1)`` + ``commit`` in one
         launch. Masks ``logits`` in place and returns the chosen tokens (int64,
         torch.argmax semantics: first maximal index)."""
-        slots = self._slots(seq_ids)
+        slots, slot_ptr = self._slots_arg(seq_ids)
         B = int(slots.numel())
         if int(logits.shape[0]) != B:
             raise RuntimeError("bpdecode_b200: one logits row per seq_id")
@@ -438,7 +446,7 @@ class ConstraintBatch:
         L = _capi.lib()
         L.check(L.bpd_dense_step_greedy(
             logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
-            slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1],
+            slot_ptr, t.allow_bits.data_ptr(), t.allow_bits.shape[1],
             t.tok_next.data_ptr(), t.num_states, float(neg_inf), tokens.data_ptr(), None,
             int(chunks_per_row), self._scratch.data_ptr(), _stream(logits)))
         return tokens
@@ -456,7 +464,7 @@ class ConstraintBatch:
         t = self._t
         if t.lookahead is None:
             raise ValueError("fsa has no lookahead table; build with dense + with_lookahead")
-        slots = self._slots(seq_ids)
+        slots, slot_ptr = self._slots_arg(seq_ids)
         B = int(slots.numel())
         if int(logits.shape[0]) != B:
             raise RuntimeError("bpdecode_b200: one logits row per seq_id")
@@ -465,7 +473,7 @@ class ConstraintBatch:
         L = _capi.lib()
         L.check(L.bpd_soft_step_greedy(
             logits.data_ptr(), code, logits.stride(0), B, t.vocab_size, self._state.data_ptr(),
-            slots.data_ptr(), t.lookahead.data_ptr(), t.allow_bits.data_ptr(),
+            slot_ptr, t.lookahead.data_ptr(), t.allow_bits.data_ptr(),
             t.allow_bits.shape[1], t.tok_next.data_ptr(), t.num_states, float(alpha),
             tokens.data_ptr(), None, int(chunks_per_row), self._scratch.data_ptr(),
             _stream(logits)))
@@ -485,7 +493,7 @@ class ConstraintBatch:
         dtype; rows 0..B-1 when ``src_rows`` is None), the masked fp32 row goes
         to ``out[b]`` (None: nowhere), ``src`` is not modified. Returns the
         tokens (int64)."""
-        slots = self._slots(seq_ids)
+        slots, slot_ptr = self._slots_arg(seq_ids)
         B = int(slots.numel())
         t = self._t
         code, rows, out = _source_args(src, t.vocab_size, B, src_rows, out, self.device)
@@ -494,7 +502,7 @@ class ConstraintBatch:
         L.check(L.bpd_dense_step_greedy_from(
             src.data_ptr(), code, src.stride(0), _ptr(rows), _ptr(out),
             out.stride(0) if out is not None else 0, B, t.vocab_size, self._state.data_ptr(),
-            slots.data_ptr(), t.allow_bits.data_ptr(), t.allow_bits.shape[1],
+            slot_ptr, t.allow_bits.data_ptr(), t.allow_bits.shape[1],
             t.tok_next.data_ptr(), t.num_states, float(neg_inf), tokens.data_ptr(), None,
             int(chunks_per_row), self._scratch.data_ptr(), _stream(src)))
         return tokens

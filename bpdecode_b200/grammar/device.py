@@ -418,16 +418,24 @@ class CFGConstraintBatch:
 
     # --- per-step ------------------------------------------------------
     def _slots(self, seq_ids: Sequence[Hashable]) -> torch.Tensor:
+        return self._slots_arg(seq_ids)[0]
+
+    def _slots_arg(self, seq_ids: Sequence[Hashable]) -> tuple[torch.Tensor, int | None]:
+        """The device slot tensor of ``seq_ids`` and the pointer the kernels
+        get for it: None when row b is slot b for every row (the kernels then
+        skip the slot load)."""
         key = seq_ids if isinstance(seq_ids, tuple) else tuple(seq_ids)
         hit = self._slot_cache.get(key)
         if hit is not None:
             self._slot_cache.move_to_end(key)
             return hit
-        slots = _upload([self._slot_of[s] for s in key], torch.int64, self.device)
-        self._slot_cache[key] = slots
+        host = [self._slot_of[s] for s in key]
+        slots = _upload(host, torch.int64, self.device)
+        hit = (slots, None if all(s == i for i, s in enumerate(host)) else slots.data_ptr())
+        self._slot_cache[key] = hit
         if len(self._slot_cache) > self._SLOT_CACHE:
             self._slot_cache.popitem(last=False)
-        return slots
+        return hit
 
     def apply_mask(self, seq_ids: Sequence[Hashable], logits: torch.Tensor,
                    neg_inf: float = float("-inf")) -> torch.Tensor:
@@ -461,7 +469,7 @@ class CFGConstraintBatch:
         argmax fused into the masking pass. Masks ``logits`` in place, commits
         the first maximal token of every row and returns those tokens (int64);
         the per-row commit status is kept in ``last_status``."""
-        slots = self._slots(seq_ids)
+        slots, slot_ptr = self._slots_arg(seq_ids)
         B = int(slots.numel())
         if int(logits.shape[0]) != B:
             raise RuntimeError("bpdecode_b200: one logits row per seq_id")
@@ -473,7 +481,7 @@ class CFGConstraintBatch:
         L = _capi.lib()
         L.check(L.bpd_pda_step_greedy(
             C.byref(self.g._struct()), logits.data_ptr(), code, logits.stride(0),
-            self._configs.data_ptr(), slots.data_ptr(), self._broken.view(torch.uint8).data_ptr(),
+            self._configs.data_ptr(), slot_ptr, self._broken.view(torch.uint8).data_ptr(),
             B, mbuf.data_ptr(), cap, ws.data_ptr(), float(neg_inf), tokens.data_ptr(),
             status.data_ptr(), int(chunks_per_row), _stream(logits)))
         self.last_status = status

@@ -120,10 +120,10 @@ size_t bpd_step_scratch_bytes(int32_t batch);
  * masked row (first maximal index, NaN counts as maximal, like torch.argmax)
  * + commit of that token (as bpd_dense_advance with write_back = 1).
  * token_out int64 [batch]; next_out int32 [batch] may be NULL.
- * A persistent grid takes (row, chunk) items from an atomic counter;
- * chunks_per_row (0 = automatic, else 1..4096) sets how many items a row is
- * cut into. step_scratch: bpd_step_scratch_bytes(batch) bytes, 16-byte
- * aligned. */
+ * One CTA per (row, chunk); chunks_per_row (0 = automatic, else 1..4096)
+ * sets how many chunks a row is cut into. slots may be NULL (row b uses
+ * state_pool[b]). step_scratch: bpd_step_scratch_bytes(batch) bytes,
+ * 16-byte aligned. */
 bpd_status bpd_dense_step_greedy(
     void* logits, int32_t dtype, int64_t row_stride, int32_t batch,
     int32_t vocab_size, int32_t* state_pool, const int64_t* slots,
