@@ -300,16 +300,19 @@ def run_config5(args: argparse.Namespace) -> None:
     """Config 5, per GPU: 1024 rows of continuous batching at V = 128,256 --
     50 % regex requests (the 8 patterns), 30 % the JSON-Schema object (dense
     DFA), 20 % the recursive JSON-value grammar (PDA); the dense rows are
-    scored with the horizon-4 soft lookahead on an fp32 copy of their bf16
-    logits, all rows greedy; every step 10 % of the requests are retired and
-    new ones admitted in their rows (bpdecode_b200.serving.MixedServingLoop).
-    Timed: --steps steps (default 1000), each = the fused steps of both paths
-    + the turnover, CUDA events around the whole loop (host bookkeeping
-    included), max over ranks."""
+    scored with the horizon-4 soft lookahead on fp32 working values read from
+    their bf16 logits, all rows greedy; every step each request retires with
+    probability 0.1 and a new one is admitted in its row
+    (bpdecode_b200.serving.DeviceServingLoop: the turnover runs on the device,
+    so a whole step -- both fused steps, the tokens in row order, the
+    turnover -- is replayed from a CUDA graph, one per logits buffer).
+    Timed: --steps steps, CUDA events around the replays, max over ranks.
+    Side measurement: the same workload through MixedServingLoop (turnover
+    bookkeeping on the host, eager launches)."""
     from bpdecode_b200 import shard, tables
     from bpdecode_b200.grammar.device import PdaTensors
     from bpdecode_b200.ops import FsaTensors
-    from bpdecode_b200.serving import MixedServingLoop
+    from bpdecode_b200.serving import DeviceServingLoop, MixedServingLoop
     from bpdecode_b200.workloads import DENSE_PATTERNS, vocab_large
 
     rank, world, local = _dist()
@@ -325,13 +328,15 @@ def run_config5(args: argparse.Namespace) -> None:
     pda = PdaTensors.from_arrays(tables.load_pda("jsonvalue"), vocab, device)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
-    loop = MixedServingLoop(ROWS_PER_GPU, dense, pda, n_regex=len(DENSE_PATTERNS),
-                            seed=rank * 7 + 1)
+    block = my_block(rank, world)
+    loop = DeviceServingLoop(ROWS_PER_GPU, dense, pda, n_regex=len(DENSE_PATTERNS),
+                             seed=block * 7 + 1)
     ring = 16
-    bufs = [gen_logits(rank, 20_000 + i, device) for i in range(ring)]
+    bufs = [gen_logits(block, 20_000 + i, device) for i in range(ring)]
     for i in range(args.warmup):
         loop.step(bufs[i % ring])
         loop.turnover()
+    graphs = [loop.graph(b) for b in bufs]
     torch.cuda.synchronize()
     shard.barrier()
     a = torch.cuda.Event(enable_timing=True)
@@ -340,13 +345,28 @@ def run_config5(args: argparse.Namespace) -> None:
     with ClockSampler(local) as clocks:
         a.record()
         for i in range(steps):
-            loop.step(bufs[i % ring])
-            loop.turnover()
+            graphs[i % ring].replay()
         b.record()
         torch.cuda.synchronize()
     shard.barrier()
     ms = shard.max_over_ranks([a.elapsed_time(b)], device)[0]
-    d_rows = int((loop.kind == 0).sum())
+    pda_rows = int(loop.counts[1])
+    del graphs
+    # the host-bookkeeping loop on the same workload, eager
+    host = MixedServingLoop(ROWS_PER_GPU, dense, pda, n_regex=len(DENSE_PATTERNS),
+                            seed=block * 7 + 1)
+    hsteps = min(steps, 200)
+    for i in range(3):
+        host.step(bufs[i % ring])
+        host.turnover()
+    torch.cuda.synchronize()
+    a.record()
+    for i in range(hsteps):
+        host.step(bufs[i % ring])
+        host.turnover()
+    b.record()
+    torch.cuda.synchronize()
+    host_ms = shard.max_over_ranks([a.elapsed_time(b)], device)[0] / hsteps
     line = {
         "metric": "constrained row-steps/sec (config 5 continuous batching)",
         "value": ROWS_PER_GPU * world * steps / (ms / 1e3), "unit": UNIT, "n_gpus": world,
@@ -356,15 +376,21 @@ def run_config5(args: argparse.Namespace) -> None:
         "config": {"workload": "config 5: 1024 rows per GPU, V=128256, 50% regex (8 patterns) / "
                                "30% JSON-Schema object (dense DFA) / 20% recursive JSON-value "
                                "GBNF (PDA), soft lookahead k=4 fp32 on the dense rows, greedy, "
-                               "10% of requests retired and admitted every step",
+                               "every request retires with probability 0.1 per step and a new "
+                               "one is admitted in its row",
                    "rows_per_gpu": ROWS_PER_GPU, "global_batch": ROWS_PER_GPU * world,
                    "parallelism": f"dp{world} (rows sharded by request, no collective)",
-                   "dense_rows_at_end": d_rows, "pda_rows_at_end": ROWS_PER_GPU - d_rows,
+                   "pda_rows_at_end": pda_rows, "dense_rows_at_end": ROWS_PER_GPU - pda_rows,
                    "l2": f"{ring} logits buffers of 262 MB cycled (larger than L2)",
                    "table_build_s": build_s},
         "clocks": clocks.summary(),
-        "timing": "CUDA events around the whole loop, host bookkeeping of the turnover "
-                  "included; max over ranks",
+        "gpu_launches": steps * 6,
+        "timing": "CUDA events around the graph replays (a step = dense soft step, PDA "
+                  "mask pipeline + step, token gather, device turnover); max over ranks",
+        "host_turnover_loop": {"ms_per_step": host_ms,
+                               "value": ROWS_PER_GPU * world / (host_ms / 1e3),
+                               "path": "MixedServingLoop: exact 10 % turnover with host "
+                                       "bookkeeping, eager launches, " + f"{hsteps} steps"},
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -68,6 +68,14 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
                                          _P, _I32, _P, _I32, _F, _P, _P, _I32, _P, _P]),
     "bpd_pda_step_greedy_from": (_I32, [C.POINTER(PdaGrammar), _P, _I32, _I64, _P, _P, _I64, _P,
                                         _P, _P, _I32, _P, _I32, _P, _F, _P, _P, _I32, _P]),
+    "bpd_soft_step_greedy_from_n": (_I32, [_P, _I32, _I64, _P, _P, _I64, _I32, _P, _I32, _P, _P,
+                                           _P, _P, _I32, _P, _I32, _F, _P, _P, _I32, _P, _P]),
+    "bpd_pda_step_greedy_from_n": (_I32, [C.POINTER(PdaGrammar), _P, _I32, _I64, _P, _P, _I64,
+                                          _P, _P, _P, _I32, _P, _P, _I32, _P, _F, _P, _P, _I32,
+                                          _P]),
+    "bpd_serving_turnover": (_I32, [_I32, C.c_uint64, _P, _F, _F, _F, _I32, _I32, _P, _P, _P, _P,
+                                    _P, _P, _P, _P, _P, _P, _P]),
+    "bpd_serving_gather_tokens": (_I32, [_I32, _P, _P, _P, _P, _P, _P, _P]),
     "bpd_pda_init": (_I32, [C.POINTER(PdaGrammar), _P, _P]),
     "bpd_pda_memo_bytes": (_S, [_I32, _I32]),
     "bpd_pda_memo_reset": (_I32, [_P, _I32, _I32, _P]),

@@ -836,11 +836,12 @@ constexpr int kLookupWarps = 4;
 __global__ void __launch_bounds__(kLookupWarps * 32)
     lookup_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
                   const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
-                  int32_t batch, Memo memo, Work w) {
+                  int32_t batch, Memo memo, Work w, const int32_t* __restrict__ nrows) {
   __shared__ int32_t buf[kLookupWarps][2][NCFG];
   const int warp = threadIdx.x >> 5;
   const int32_t b = blockIdx.x * kLookupWarps + warp;
-  if (b < batch) lookup_row(g, pool, slots, broken, b, memo, w, buf[warp][0], buf[warp][1]);
+  const int32_t n = nrows != nullptr ? min(batch, *nrows) : batch;
+  if (b < n) lookup_row(g, pool, slots, broken, b, memo, w, buf[warp][0], buf[warp][1]);
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -877,8 +878,24 @@ __device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work
 // Row -> its allow words through the memo / workspace (nullptr for broken rows).
 struct PdaRows {
   static constexpr bool kSoft = false;
+  struct Pre {
+    int32_t kind, ref;
+  };
   Memo memo;
   Work w;
+  __device__ __forceinline__ Pre pre(int32_t row) const { return Pre{w.kind[row], w.ref[row]}; }
+  __device__ __forceinline__ RowInfo info(int32_t row, const Pre& p) const {
+    const uint32_t* b = nullptr;
+    if (p.kind == kHit) {
+      b = memo.bits + static_cast<int64_t>(p.ref) * memo.ws;
+    } else if (p.kind == kRep) {
+      b = (memo.cap && p.ref >= 0) ? memo.bits + static_cast<int64_t>(p.ref) * memo.ws
+                                   : w.bits + static_cast<int64_t>(row) * memo.ws;
+    } else if (p.kind == kAlias) {
+      b = rep_bits(memo, w, p.ref);
+    }
+    return RowInfo{b, 0, 0};
+  }
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {
     return RowInfo{row_bits(memo, w, row), 0, 0};
   }
@@ -1012,7 +1029,8 @@ bpd_status check_grammar(const bpd_pda_grammar* g) {
 // resolvable through (memo, work).
 bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, const int64_t* slots,
                              const uint8_t* broken, int32_t batch, void* memo_mem, int32_t cap,
-                             void* workspace, Memo* memo_out, Work* work_out, cudaStream_t st) {
+                             void* workspace, Memo* memo_out, Work* work_out, cudaStream_t st,
+                             const int32_t* nrows = nullptr) {
   bpd_status rc = check_grammar(g);
   if (rc) return rc;
   BPD_REQUIRE(pool && workspace, "null config pool or workspace");
@@ -1023,7 +1041,7 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
   cudaError_t e = cudaMemsetAsync(w.dedup, 0, w.clear_bytes, st);
   if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memset dedup: %s", cudaGetErrorString(e));
   lookup_kernel<<<(batch + kLookupWarps - 1) / kLookupWarps, kLookupWarps * 32, 0, st>>>(
-      *g, pool, slots, broken, batch, memo, w);
+      *g, pool, slots, broken, batch, memo, w, nrows);
   rc = check_launch("pda lookup_kernel");
   if (rc) return rc;
   const int32_t sms = sm_count();
@@ -1166,36 +1184,63 @@ extern "C" bpd_status bpd_pda_step_greedy(
   });
 }
 
+namespace bpd {
+namespace {
+bpd_status pda_step_from(
+    const bpd_pda_grammar* g, const void* src, int32_t src_dtype, int64_t src_stride,
+    const int64_t* src_rows, float* out, int64_t out_stride, int32_t* config_pool,
+    const int64_t* slots, uint8_t* broken, int32_t batch, void* memo, int32_t memo_capacity,
+    void* workspace, float neg_inf, int64_t* token_out, int32_t* status_out,
+    int32_t chunks_per_row, void* stream, const int32_t* nrows, const char* what) {
+  BPD_REQUIRE(batch >= 0, "%s: bad batch", what);
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(src != nullptr && token_out != nullptr, "%s: null pointer", what);
+  BPD_REQUIRE(g && src_stride >= g->vocab_size &&
+                  (out == nullptr || out_stride >= g->vocab_size),
+              "%s: row stride < vocab", what);
+  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
+              "%s: chunks_per_row must be in [0, 4096]", what);
+  cudaStream_t st = as_stream(stream);
+  Memo m;
+  Work w;
+  bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
+                                    workspace, &m, &w, st, nrows);
+  if (rc) return rc;
+  const PdaCommit commit{*g, config_pool, slots, token_out, broken, status_out};
+  const PdaRows rows{m, w};
+  const int32_t V = g->vocab_size;
+  return with_dtype(src_dtype, what, [&](auto tag) {
+    using T = decltype(tag);
+    return launch_stream_step_src<T, PdaRows, PdaCommit>(
+        src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
+        chunks_per_row, w.step, st, what, nrows);
+  }, "source");
+}
+}  // namespace
+}  // namespace bpd
+
 extern "C" bpd_status bpd_pda_step_greedy_from(
     const bpd_pda_grammar* g, const void* src, int32_t src_dtype, int64_t src_stride,
     const int64_t* src_rows, float* out, int64_t out_stride, int32_t* config_pool,
     const int64_t* slots, uint8_t* broken, int32_t batch, void* memo, int32_t memo_capacity,
     void* workspace, float neg_inf, int64_t* token_out, int32_t* status_out,
     int32_t chunks_per_row, void* stream) {
-  BPD_REQUIRE(batch >= 0, "bpd_pda_step_greedy_from: bad batch");
-  if (batch == 0) return BPD_OK;
-  BPD_REQUIRE(src != nullptr && token_out != nullptr, "bpd_pda_step_greedy_from: null pointer");
-  BPD_REQUIRE(g && src_stride >= g->vocab_size &&
-                  (out == nullptr || out_stride >= g->vocab_size),
-              "bpd_pda_step_greedy_from: row stride < vocab");
-  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
-              "bpd_pda_step_greedy_from: chunks_per_row must be in [0, 4096]");
-  cudaStream_t st = as_stream(stream);
-  Memo m;
-  Work w;
-  bpd_status rc = run_mask_pipeline(g, config_pool, slots, broken, batch, memo, memo_capacity,
-                                    workspace, &m, &w, st);
-  if (rc) return rc;
-  const PdaCommit commit{*g, config_pool, slots, token_out, broken, status_out};
-  const PdaRows rows{m, w};
-  const int32_t V = g->vocab_size;
-  const char* what = "bpd_pda_step_greedy_from";
-  return with_dtype(src_dtype, what, [&](auto tag) {
-    using T = decltype(tag);
-    return launch_stream_step_src<T, PdaRows, PdaCommit>(
-        src, src_stride, src_rows, out, out_stride, batch, V, rows, commit, neg_inf,
-        chunks_per_row, w.step, st, what);
-  }, "source");
+  return pda_step_from(g, src, src_dtype, src_stride, src_rows, out, out_stride, config_pool,
+                       slots, broken, batch, memo, memo_capacity, workspace, neg_inf, token_out,
+                       status_out, chunks_per_row, stream, nullptr, "bpd_pda_step_greedy_from");
+}
+
+extern "C" bpd_status bpd_pda_step_greedy_from_n(
+    const bpd_pda_grammar* g, const void* src, int32_t src_dtype, int64_t src_stride,
+    const int64_t* src_rows, float* out, int64_t out_stride, int32_t* config_pool,
+    const int64_t* slots, uint8_t* broken, int32_t batch, const int32_t* batch_dev, void* memo,
+    int32_t memo_capacity, void* workspace, float neg_inf, int64_t* token_out,
+    int32_t* status_out, int32_t chunks_per_row, void* stream) {
+  BPD_REQUIRE(batch_dev != nullptr, "bpd_pda_step_greedy_from_n: null row count");
+  return pda_step_from(g, src, src_dtype, src_stride, src_rows, out, out_stride, config_pool,
+                       slots, broken, batch, memo, memo_capacity, workspace, neg_inf, token_out,
+                       status_out, chunks_per_row, stream, batch_dev,
+                       "bpd_pda_step_greedy_from_n");
 }
 
 extern "C" bpd_status bpd_pda_advance(const bpd_pda_grammar* g, int32_t* config_pool,

@@ -109,6 +109,7 @@ __global__ void lookahead_out_kernel(const int32_t* __restrict__ tn, int32_t S, 
 // live) and its lookahead row (the biases); no state = everything -inf.
 struct SoftRows {
   static constexpr bool kSoft = true;
+  using Pre = StatePre;
   const int32_t* pool;
   const int64_t* slots;
   const uint32_t* bits;
@@ -117,6 +118,16 @@ struct SoftRows {
   int32_t S;
   int32_t V;
   float alpha;
+  __device__ __forceinline__ Pre pre(int32_t row) const { return state_pre(pool, slots, row); }
+  __device__ __forceinline__ RowInfo info(int32_t, const Pre& p) const {
+    RowInfo r;
+    r.state = p.state;
+    r.slot = p.slot;
+    const bool ok = p.state >= 0 && p.state < S;
+    r.brow = ok ? bits + static_cast<int64_t>(p.state) * wstride : nullptr;
+    r.lrow = ok ? la + static_cast<int64_t>(p.state) * V : nullptr;
+    return r;
+  }
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {
     RowInfo r;
     r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);
@@ -226,6 +237,39 @@ extern "C" bpd_status bpd_soft_step_greedy(void* logits, int32_t dtype, int64_t 
   });
 }
 
+namespace bpd {
+namespace {
+bpd_status soft_step_from(
+    const void* src, int32_t src_dtype, int64_t src_stride, const int64_t* src_rows,
+    float* out, int64_t out_stride, int32_t batch, int32_t vocab_size, int32_t* state_pool,
+    const int64_t* slots, const float* lookahead, const uint32_t* allow_bits,
+    int32_t words_stride, const int32_t* tok_next, int32_t num_states, float alpha,
+    int64_t* token_out, int32_t* next_out, int32_t chunks_per_row, void* step_scratch,
+    void* stream, const int32_t* nrows, const char* what) {
+  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "%s: bad sizes", what);
+  if (batch == 0) return BPD_OK;
+  BPD_REQUIRE(src && state_pool && lookahead && allow_bits && tok_next && token_out,
+              "%s: null pointer", what);
+  BPD_REQUIRE(src_stride >= vocab_size && (out == nullptr || out_stride >= vocab_size),
+              "%s: row stride < vocab", what);
+  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
+              "%s: words_stride too small", what);
+  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
+              "%s: chunks_per_row must be in [0, 4096]", what);
+  cudaStream_t st = as_stream(stream);
+  const SoftRows rows{state_pool, slots, allow_bits, words_stride, lookahead, num_states,
+                      vocab_size, alpha};
+  const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
+  return with_dtype(src_dtype, what, [&](auto tag) {
+    using T = decltype(tag);
+    return launch_stream_step_src<T, SoftRows, DenseCommit>(
+        src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
+        chunks_per_row, step_scratch, st, what, nrows);
+  }, "source");
+}
+}  // namespace
+}  // namespace bpd
+
 extern "C" bpd_status bpd_soft_step_greedy_from(
     const void* src, int32_t src_dtype, int64_t src_stride, const int64_t* src_rows,
     float* out, int64_t out_stride, int32_t batch, int32_t vocab_size, int32_t* state_pool,
@@ -233,25 +277,22 @@ extern "C" bpd_status bpd_soft_step_greedy_from(
     int32_t words_stride, const int32_t* tok_next, int32_t num_states, float alpha,
     int64_t* token_out, int32_t* next_out, int32_t chunks_per_row, void* step_scratch,
     void* stream) {
-  BPD_REQUIRE(batch >= 0 && vocab_size > 0, "bpd_soft_step_greedy_from: bad sizes");
-  if (batch == 0) return BPD_OK;
-  BPD_REQUIRE(src && state_pool && lookahead && allow_bits && tok_next && token_out,
-              "bpd_soft_step_greedy_from: null pointer");
-  BPD_REQUIRE(src_stride >= vocab_size && (out == nullptr || out_stride >= vocab_size),
-              "bpd_soft_step_greedy_from: row stride < vocab");
-  BPD_REQUIRE(words_stride >= (vocab_size + 31) / 32,
-              "bpd_soft_step_greedy_from: words_stride too small");
-  BPD_REQUIRE(chunks_per_row >= 0 && chunks_per_row <= 4096,
-              "bpd_soft_step_greedy_from: chunks_per_row must be in [0, 4096]");
-  cudaStream_t st = as_stream(stream);
-  const SoftRows rows{state_pool, slots, allow_bits, words_stride, lookahead, num_states,
-                      vocab_size, alpha};
-  const DenseCommit commit{state_pool, tok_next, num_states, vocab_size, token_out, next_out};
-  const char* what = "bpd_soft_step_greedy_from";
-  return with_dtype(src_dtype, what, [&](auto tag) {
-    using T = decltype(tag);
-    return launch_stream_step_src<T, SoftRows, DenseCommit>(
-        src, src_stride, src_rows, out, out_stride, batch, vocab_size, rows, commit, -INFINITY,
-        chunks_per_row, step_scratch, st, what);
-  }, "source");
+  return soft_step_from(src, src_dtype, src_stride, src_rows, out, out_stride, batch, vocab_size,
+                        state_pool, slots, lookahead, allow_bits, words_stride, tok_next,
+                        num_states, alpha, token_out, next_out, chunks_per_row, step_scratch,
+                        stream, nullptr, "bpd_soft_step_greedy_from");
+}
+
+extern "C" bpd_status bpd_soft_step_greedy_from_n(
+    const void* src, int32_t src_dtype, int64_t src_stride, const int64_t* src_rows,
+    float* out, int64_t out_stride, int32_t batch, const int32_t* batch_dev, int32_t vocab_size,
+    int32_t* state_pool, const int64_t* slots, const float* lookahead,
+    const uint32_t* allow_bits, int32_t words_stride, const int32_t* tok_next,
+    int32_t num_states, float alpha, int64_t* token_out, int32_t* next_out,
+    int32_t chunks_per_row, void* step_scratch, void* stream) {
+  BPD_REQUIRE(batch_dev != nullptr, "bpd_soft_step_greedy_from_n: null row count");
+  return soft_step_from(src, src_dtype, src_stride, src_rows, out, out_stride, batch, vocab_size,
+                        state_pool, slots, lookahead, allow_bits, words_stride, tok_next,
+                        num_states, alpha, token_out, next_out, chunks_per_row, step_scratch,
+                        stream, batch_dev, "bpd_soft_step_greedy_from_n");
 }

@@ -7,6 +7,7 @@
 // mixed -> load, blend, store.
 #pragma once
 
+#include <algorithm>
 #include <climits>
 #include <type_traits>
 
@@ -658,13 +659,40 @@ __device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__
   return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
 }
 
+// A Rows functor gives a row's RowInfo in two steps, so that a persistent
+// warp can issue the loads for its next row while it streams the current
+// one: pre(row) only loads (its results are consumed later), info(row, pre)
+// does the arithmetic. operator()(row) is both at once.
+struct StatePre {
+  int64_t slot;
+  int32_t state;
+};
+
+__device__ __forceinline__ StatePre state_pre(const int32_t* __restrict__ pool,
+                                              const int64_t* __restrict__ slots, int32_t row) {
+  StatePre p;
+  p.slot = slots ? slots[row] : row;
+  p.state = pool[p.slot];
+  return p;
+}
+
 struct DenseRows {
   static constexpr bool kSoft = false;
+  using Pre = StatePre;
   const int32_t* pool;
   const int64_t* slots;
   const uint32_t* bits;
   int32_t wstride;
   int32_t S;
+  __device__ __forceinline__ Pre pre(int32_t row) const { return state_pre(pool, slots, row); }
+  __device__ __forceinline__ RowInfo info(int32_t, const Pre& p) const {
+    RowInfo r;
+    r.state = p.state;
+    r.slot = p.slot;
+    r.brow = (p.state >= 0 && p.state < S) ? bits + static_cast<int64_t>(p.state) * wstride
+                                           : nullptr;
+    return r;
+  }
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {
     RowInfo r;
     r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);
@@ -824,25 +852,29 @@ __global__ void __launch_bounds__(kThreads, staged_path<kVec, true, Rows>()
 }
 
 // Device scratch of the fused step: per row the best packed (key, ~index) so
-// far and the number of warps done. It must be zero before a launch; every
-// launch that runs to completion leaves it zero again (the row's last warp
-// clears it).
+// far and the number of pieces done, and the persistent kernel's work queue
+// (next item, warps finished). It must be zero before a launch; every launch
+// that runs to completion leaves it zero again (the row's last piece clears
+// the row's words, the last warp out clears the queue).
 struct StepScratch {
   unsigned long long* best;  // [batch]
   uint32_t* done;            // [batch]
+  uint32_t* queue;           // [2]
 };
 
 constexpr size_t step_scratch_bytes(int32_t batch) {
   return align256(sizeof(unsigned long long) * static_cast<size_t>(batch)) +
-         align256(sizeof(uint32_t) * static_cast<size_t>(batch));
+         align256(sizeof(uint32_t) * static_cast<size_t>(batch)) + 256;
 }
 
 inline StepScratch step_scratch_view(void* base, int32_t batch) {
   char* p = static_cast<char*>(base);
   StepScratch s;
   s.best = reinterpret_cast<unsigned long long*>(p);
-  s.done = reinterpret_cast<uint32_t*>(
-      p + align256(sizeof(unsigned long long) * static_cast<size_t>(batch)));
+  p += align256(sizeof(unsigned long long) * static_cast<size_t>(batch));
+  s.done = reinterpret_cast<uint32_t*>(p);
+  p += align256(sizeof(uint32_t) * static_cast<size_t>(batch));
+  s.queue = reinterpret_cast<uint32_t*>(p);
   return s;
 }
 
@@ -865,10 +897,13 @@ __global__ void __launch_bounds__(kThreads,
     stream_step_kernel(T* __restrict__ logits, int64_t row_stride, const S* __restrict__ src,
                        int64_t src_stride, const int64_t* __restrict__ src_rows, int32_t V,
                        Rows rows, Commit commit, typename Dt<T>::Bits fill, int32_t chunk,
-                       int32_t chunks_per_row, StepScratch ws) {
+                       int32_t chunks_per_row, StepScratch ws,
+                       const int32_t* __restrict__ nrows) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ unsigned long long warp_q[kWarps];
   __shared__ uint32_t warps_done;
+  // rows at or past a device-held row count are not part of this call
+  if (nrows != nullptr && static_cast<int32_t>(blockIdx.x / chunks_per_row) >= *nrows) return;
   if (threadIdx.x == 0) warps_done = 0u;
   if constexpr (kVec) fill_init<T>(smem, fill);
   __syncthreads();
@@ -964,6 +999,187 @@ bpd_status allow_smem(size_t bytes, const char* what) {
   return BPD_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Persistent fused step: a grid of resident CTAs whose WARPS take work items
+// -- (row, segment of seg_tiles warp tiles) -- from an atomic queue. The CTA
+// fills its shared fill buffer once for the whole launch; each warp fetches
+// its next item index one item ahead and issues the loads of that item's
+// row (Rows::pre) before it streams the current one, so the dependent chain
+// of a row (slot -> state -> allow row) overlaps the streaming instead of
+// preceding it. A row's pieces meet as in stream_step_kernel: one 64-bit
+// atomicMax per piece and an acquire-release count; the warp that completes
+// the row commits it. Nothing waits on another warp or CTA; the last warp to
+// finish resets the queue (release fence before each warp's exit count).
+//
+// The last segment of a row also takes its ragged end (V mod TILE elements,
+// one per lane). Segments past the row's tiles (chunks_per_row larger than
+// the tile count) are empty pieces that still count.
+#ifndef BPD_PERSIST
+#define BPD_PERSIST 1
+#endif
+#ifndef BPD_PERSIST_BLOCKS
+#define BPD_PERSIST_BLOCKS 5
+#endif
+#ifndef BPD_SEG_TILES
+#define BPD_SEG_TILES 8
+#endif
+
+template <typename T, typename S, bool kInPlace, class Rows, class Commit>
+__global__ void __launch_bounds__(kThreads, BPD_PERSIST_BLOCKS)
+    persist_step_kernel(T* __restrict__ logits, int64_t row_stride, const S* __restrict__ src,
+                        int64_t src_stride, const int64_t* __restrict__ src_rows, int32_t V,
+                        Rows rows, Commit commit, typename Dt<T>::Bits fill, int32_t seg_tiles,
+                        int32_t segs_per_row, int32_t items, StepScratch ws,
+                        const int32_t* __restrict__ nrows) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int32_t TILE = tile_elems<T>();
+  fill_init<T>(smem, fill);
+  __syncthreads();
+  const uint4* sfill = reinterpret_cast<const uint4*>(smem);
+  const int32_t lane = threadIdx.x & 31;
+  uint8_t* csmem = smem + kFillBytes + (threadIdx.x >> 5) * Commit::kSmemBytes;
+  const int32_t ntr = V / TILE;  // full warp tiles of a row
+  uint32_t item = 0, nxt = 0;
+  if (lane == 0) {
+    item = atomicAdd(ws.queue, 1u);
+    nxt = atomicAdd(ws.queue, 1u);
+  }
+  item = __shfl_sync(kAll, item, 0);
+  nxt = __shfl_sync(kAll, nxt, 0);
+  // with a device-held row count, only the items of rows below it
+  const uint32_t nitems =
+      nrows == nullptr
+          ? static_cast<uint32_t>(items)
+          : static_cast<uint32_t>(min(items, max(0, min(*nrows, items / segs_per_row)) *
+                                                 segs_per_row));
+  typename Rows::Pre pre{};
+  if (item < nitems) pre = rows.pre(static_cast<int32_t>(item) / segs_per_row);
+  bool any_issued = false;
+  while (item < nitems) {
+    const int32_t row = static_cast<int32_t>(item) / segs_per_row;
+    const int32_t seg = static_cast<int32_t>(item) - row * segs_per_row;
+    // the next item's row loads and the index after it: in flight while
+    // this item streams
+    typename Rows::Pre npre{};
+    if (nxt < nitems) npre = rows.pre(static_cast<int32_t>(nxt) / segs_per_row);
+    uint32_t after = 0;
+    if (lane == 0 && nxt < nitems) after = atomicAdd(ws.queue, 1u);
+    const RowInfo info = rows.info(row, pre);
+    const int32_t t0 = seg * seg_tiles;
+    const int32_t nt = max(0, min(seg_tiles, ntr - t0));
+    const bool last = seg == segs_per_row - 1;
+    const int32_t e0 = min(t0, ntr) * TILE;
+    const int32_t s0 = ntr * TILE;
+    const int32_t s1 = last ? V : s0;
+    T* rowp = logits != nullptr ? logits + row * row_stride : nullptr;
+    const S* srow;
+    if constexpr (kInPlace) {
+      srow = rowp;
+    } else {
+      srow = src + (src_rows != nullptr ? src_rows[row] : static_cast<int64_t>(row)) * src_stride;
+    }
+    ArgState st;
+    bool issued = false;
+    warp_span<T, S, kInPlace, true, true, Rows::kSoft>(rowp, srow, e0, nt, s0, s1, info.brow,
+                                                        fill, sfill, info.lrow, rows_alpha(rows),
+                                                        st, issued);
+    any_issued = any_issued || issued;
+    const unsigned long long q = warp_max_u64(pack_arg(st.key, st.idx));
+    int32_t tok = -1;
+    if (lane == 0) {
+      if (segs_per_row == 1) {
+        tok = unpack_idx(q);
+      } else {
+        atomicMax(ws.best + row, q);
+        uint32_t arrived;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(arrived)
+                     : "l"(ws.done + row)
+                     : "memory");
+        if (arrived == static_cast<uint32_t>(segs_per_row - 1)) {
+          const unsigned long long b = atomicExch(ws.best + row, 0ull);
+          ws.done[row] = 0u;
+          tok = unpack_idx(b);
+        }
+      }
+      // bound the bulk stores this thread has in flight (their source is the
+      // read-only fill buffer, so only the count matters)
+      if (any_issued) asm volatile("cp.async.bulk.wait_group.read 8;" ::: "memory");
+    }
+    tok = __shfl_sync(kAll, tok, 0);
+    if (tok >= 0) commit(row, info, tok, csmem);
+    item = nxt;
+    nxt = __shfl_sync(kAll, after, 0);
+    pre = npre;
+  }
+  if (lane == 0) {
+    if (any_issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    // every queue fetch of this warp is ordered before its exit count; the
+    // last warp out sees all of them and clears the queue for the next launch
+    __threadfence();
+    uint32_t out;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(out)
+                 : "l"(ws.queue + 1)
+                 : "memory");
+    if (out == gridDim.x * static_cast<uint32_t>(kWarps) - 1u) {
+      ws.queue[0] = 0u;
+      ws.queue[1] = 0u;
+    }
+  }
+}
+
+// Work layout of the persistent step: warp tiles per segment and segments
+// per row. chunks_per_row > 0 sets the segment count; 0 picks BPD_SEG_TILES
+// tiles per segment, halved for small batches until there are about 4 items
+// per SM.
+struct PersistLayout {
+  int32_t seg_tiles, segs, items, grid;
+};
+
+template <typename T>
+inline PersistLayout persist_layout(int32_t V, int32_t batch, int32_t chunks_per_row) {
+  constexpr int32_t TILE = tile_elems<T>();
+  const int32_t ntr = V / TILE;
+  const int64_t sms = sm_count();
+  PersistLayout L;
+  if (chunks_per_row > 0) {
+    L.segs = chunks_per_row;
+    L.seg_tiles = max(1, (ntr + L.segs - 1) / L.segs);
+  } else {
+    L.seg_tiles = BPD_SEG_TILES;
+    while (L.seg_tiles > 1 &&
+           static_cast<int64_t>(batch) * ((ntr + L.seg_tiles - 1) / L.seg_tiles) < sms * 4)
+      L.seg_tiles /= 2;
+    L.segs = max(1, (ntr + L.seg_tiles - 1) / L.seg_tiles);
+  }
+  const int64_t items = static_cast<int64_t>(batch) * L.segs;
+  L.items = items < 0x7FFFFFFF ? static_cast<int32_t>(items) : -1;
+  L.grid = static_cast<int32_t>(std::min<int64_t>(sms * BPD_PERSIST_BLOCKS, std::max<int64_t>(items, 1)));
+  return L;
+}
+
+template <typename T, typename S, bool kInPlace, class Rows, class Commit>
+bpd_status launch_persist_step(T* out, int64_t out_stride, const S* src, int64_t src_stride,
+                               const int64_t* src_rows, int32_t batch, int32_t V,
+                               const Rows& rows, const Commit& commit,
+                               typename Dt<T>::Bits fill, int32_t chunks_per_row,
+                               const StepScratch& ws, cudaStream_t st, const char* what,
+                               const int32_t* nrows = nullptr) {
+  const PersistLayout L = persist_layout<T>(V, batch, chunks_per_row);
+  if (L.items < 0) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
+  const size_t smem = static_cast<size_t>(kFillBytes) +
+                      static_cast<size_t>(kWarps) * static_cast<size_t>(Commit::kSmemBytes);
+  const bpd_status rc =
+      allow_smem<persist_step_kernel<T, S, kInPlace, Rows, Commit>>(smem, what);
+  if (rc) return rc;
+  persist_step_kernel<T, S, kInPlace, Rows, Commit>
+      <<<static_cast<unsigned>(L.grid), kThreads, smem, st>>>(
+          out, out_stride, src, src_stride, src_rows, V, rows, commit, fill, L.seg_tiles, L.segs,
+          L.items, ws, nrows);
+  return check_launch(what);
+}
+
 inline bool rows_aligned(const void* logits, int64_t row_stride, size_t esize) {
   return aligned16(logits) && (row_stride * static_cast<int64_t>(esize)) % 16 == 0;
 }
@@ -1013,6 +1229,11 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   const StepScratch ws = step_scratch_view(scratch, batch);
   T* lg = static_cast<T*>(logits);
   const size_t smem = kFillBytes + Commit::kSmemBytes;
+  if (BPD_PERSIST && vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
+    return launch_persist_step<T, T, true, Rows, Commit>(lg, row_stride, lg, row_stride, nullptr,
+                                                         batch, V, rows, commit, fill,
+                                                         chunks_per_row, ws, st, what);
+  }
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
     constexpr size_t vsmem =
         stream_smem_bytes<staged_path<true, true, Rows>()>(Commit::kSmemBytes);
@@ -1022,12 +1243,12 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
     stream_step_kernel<T, T, true, true, Rows, Commit>
         <<<static_cast<unsigned>(grid), kThreads, vsmem, st>>>(lg, row_stride, lg, row_stride,
                                                                 nullptr, V, rows, commit, fill,
-                                                                chunk, cpr, ws);
+                                                                chunk, cpr, ws, nullptr);
   } else {
     stream_step_kernel<T, T, true, false, Rows, Commit>
         <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(lg, row_stride, lg, row_stride,
                                                                nullptr, V, rows, commit, fill,
-                                                               chunk, cpr, ws);
+                                                               chunk, cpr, ws, nullptr);
   }
   return check_launch(what);
 }
@@ -1040,7 +1261,7 @@ bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int
                                   float* out, int64_t out_stride, int32_t batch, int32_t V,
                                   const Rows& rows, const Commit& commit, float neg_inf,
                                   int32_t chunks_per_row, void* scratch, cudaStream_t st,
-                                  const char* what) {
+                                  const char* what, const int32_t* nrows = nullptr) {
   if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
   if (!aligned16(scratch))
     return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
@@ -1055,16 +1276,22 @@ bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int
                    (out == nullptr || rows_aligned(out, out_stride, sizeof(float))) &&
                    (!Rows::kSoft || V % 4 == 0);
   const S* sp = static_cast<const S*>(src);
+  if (BPD_PERSIST && vec) {
+    return launch_persist_step<float, S, false, Rows, Commit>(out, out_stride, sp, src_stride,
+                                                              src_rows, batch, V, rows, commit,
+                                                              fill, chunks_per_row, ws, st, what,
+                                                              nrows);
+  }
   if (vec) {
     stream_step_kernel<float, S, false, true, Rows, Commit>
         <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(out, out_stride, sp, src_stride,
                                                                src_rows, V, rows, commit, fill,
-                                                               chunk, cpr, ws);
+                                                               chunk, cpr, ws, nrows);
   } else {
     stream_step_kernel<float, S, false, false, Rows, Commit>
         <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(out, out_stride, sp, src_stride,
                                                                src_rows, V, rows, commit, fill,
-                                                               chunk, cpr, ws);
+                                                               chunk, cpr, ws, nrows);
   }
   return check_launch(what);
 }

@@ -28,9 +28,12 @@ from collections.abc import Sequence
 import numpy as np
 import torch
 
+import ctypes as C
+
+from . import _capi
 from .batch import FREE, ConstraintBatch
 from .grammar.device import CFGConstraintBatch, PdaTensors
-from .ops import FsaTensors
+from .ops import FsaTensors, _source_args, _stream
 
 
 class MixedServingLoop:
@@ -172,4 +175,125 @@ class MixedServingLoop:
         return self.dense._state, self.pda._configs, self.pda._broken
 
 
-__all__ = ["MixedServingLoop"]
+class DeviceServingLoop:
+    """The serving loop of :class:`MixedServingLoop` with its request
+    turnover on the device, so that a whole step -- the fused soft step of
+    the dense rows, the fused PDA step of the grammar rows, the tokens put
+    back in row order, the turnover -- is a fixed sequence of launches that
+    can be captured once and replayed from a CUDA graph (:meth:`graph`).
+
+    Row r holds one request and always uses slot r of the dense state pool
+    and of the PDA config pool. Device tensors describe the mix: ``kind``
+    (int32, 0 dense / 1 PDA), the ascending row lists ``dense_rows`` /
+    ``pda_rows`` (int64) and their lengths ``counts`` (int32 [2]), which the
+    steps read on the device (``bpd_*_step_greedy_from_n``). Every
+    :meth:`turnover` retires each row's request with probability
+    ``evict_fraction`` (a seeded counter-based hash of (seed, step, row):
+    10 % of the rows per step on average, where :class:`MixedServingLoop`
+    retires exactly 10 %) and admits a new one drawn from ``mix`` in its row
+    (``bpd_serving_turnover``); ``retired`` (uint8) marks the rows that turned
+    over. The host never reads the mix.
+
+    :meth:`step` returns ``tokens``, a buffer the next step overwrites.
+    """
+
+    def __init__(
+        self,
+        rows: int,
+        dense: Sequence[FsaTensors],
+        pda: PdaTensors,
+        *,
+        n_regex: int,
+        mix: tuple[float, float, float] = (0.5, 0.3, 0.2),
+        evict_fraction: float = 0.1,
+        alpha: float = 1.0,
+        seed: int = 0,
+    ) -> None:
+        self.rows = rows
+        self.n_regex = n_regex
+        self.mix = mix
+        self.evict_fraction = evict_fraction
+        self.alpha = alpha
+        self.seed = seed
+        self.dense = ConstraintBatch(list(dense), capacity=rows)
+        if self.dense._t.lookahead is None:
+            raise ValueError("DeviceServingLoop: every dense grammar needs a lookahead table")
+        dev = self.device = self.dense.device
+        self.pda = CFGConstraintBatch(pda, capacity=rows, device=dev)
+        self.schema = n_regex if len(self.dense.grammars) > n_regex else -1
+        i32, i64 = torch.int32, torch.int64
+        self.kind = torch.ones(rows, dtype=i32, device=dev)
+        self.dense_rows = torch.zeros(rows, dtype=i64, device=dev)
+        self.pda_rows = torch.zeros(rows, dtype=i64, device=dev)
+        self.counts = torch.zeros(2, dtype=i32, device=dev)
+        self.retired = torch.zeros(rows, dtype=torch.uint8, device=dev)
+        self.step_counter = torch.zeros(1, dtype=i64, device=dev)
+        self.tokens = torch.zeros(rows, dtype=i64, device=dev)
+        self._dtok = torch.zeros(rows, dtype=i64, device=dev)
+        self._ptok = torch.zeros(rows, dtype=i64, device=dev)
+        self._pstatus = torch.zeros(rows, dtype=i32, device=dev)
+        self._starts = torch.tensor(self.dense._t.starts, dtype=i32, device=dev)
+        self._init = self.pda.g.init_config()
+        self.dense._state.fill_(FREE)
+        self._memo = self.pda.g.mask_memo()
+        self._ws = self.pda.g.workspace(rows)
+        self._turnover(1.0)  # every row admits its first request
+
+    def _turnover(self, prob: float) -> None:
+        L = _capi.lib()
+        L.check(L.bpd_serving_turnover(
+            self.rows, self.seed & 0xFFFFFFFFFFFFFFFF, self.step_counter.data_ptr(), float(prob),
+            float(self.mix[0]), float(self.mix[1]), self.n_regex, self.schema,
+            self._starts.data_ptr(), self._init.data_ptr(), self.kind.data_ptr(),
+            self.dense._state.data_ptr(), self.pda._configs.data_ptr(),
+            self.pda._broken.view(torch.uint8).data_ptr(), self.dense_rows.data_ptr(),
+            self.pda_rows.data_ptr(), self.counts.data_ptr(), self.retired.data_ptr(),
+            _stream(self.kind)))
+
+    def turnover(self) -> None:
+        """Retire and admit requests (on the device, nothing read back)."""
+        self._turnover(self.evict_fraction)
+
+    def step(self, logits: torch.Tensor) -> torch.Tensor:
+        """Greedy tokens (``tokens``, int64 ``[rows]``) for ``logits``
+        (``[rows, V]``, any float dtype; not modified)."""
+        R = self.rows
+        t = self.dense._t
+        code, _, _ = _source_args(logits, t.vocab_size, R, self.dense_rows, None, self.device)
+        st = _stream(logits)
+        L = _capi.lib()
+        L.check(L.bpd_soft_step_greedy_from_n(
+            logits.data_ptr(), code, logits.stride(0), self.dense_rows.data_ptr(), None, 0, R,
+            self.counts.data_ptr(), t.vocab_size, self.dense._state.data_ptr(),
+            self.dense_rows.data_ptr(), t.lookahead.data_ptr(), t.allow_bits.data_ptr(),
+            t.allow_bits.shape[1], t.tok_next.data_ptr(), t.num_states, float(self.alpha),
+            self._dtok.data_ptr(), None, 0, self.dense._scratch.data_ptr(), st))
+        mbuf, cap = self._memo
+        L.check(L.bpd_pda_step_greedy_from_n(
+            C.byref(self.pda.g._struct()), logits.data_ptr(), code, logits.stride(0),
+            self.pda_rows.data_ptr(), None, 0, self.pda._configs.data_ptr(),
+            self.pda_rows.data_ptr(), self.pda._broken.view(torch.uint8).data_ptr(), R,
+            self.counts.data_ptr() + 4, mbuf.data_ptr(), cap, self._ws.data_ptr(),
+            float("-inf"), self._ptok.data_ptr(), self._pstatus.data_ptr(), 0, st))
+        L.check(L.bpd_serving_gather_tokens(
+            R, self.dense_rows.data_ptr(), self.pda_rows.data_ptr(), self.counts.data_ptr(),
+            self._dtok.data_ptr(), self._ptok.data_ptr(), self.tokens.data_ptr(), st))
+        return self.tokens
+
+    def graph(self, logits: torch.Tensor) -> torch.cuda.CUDAGraph:
+        """A CUDA graph of :meth:`step` on ``logits`` (this buffer; refill it
+        before each replay) followed by :meth:`turnover`. Call :meth:`step`
+        once before the first capture (it loads the kernels and sets their
+        shared-memory limits, which a capture cannot)."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step(logits)
+            self.turnover()
+        return g
+
+    def states(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(dense state pool, PDA config pool, PDA broken flags) -- row r at index r."""
+        return self.dense._state, self.pda._configs, self.pda._broken
+
+
+__all__ = ["DeviceServingLoop", "MixedServingLoop"]

@@ -235,6 +235,20 @@ bpd_status bpd_soft_step_greedy_from(
     int32_t num_states, float alpha, int64_t* token_out, int32_t* next_out,
     int32_t chunks_per_row, void* step_scratch, void* stream);
 
+/* NEW: bpd_soft_step_greedy_from over the first *batch_dev rows only, where
+ * batch_dev (int32, device memory) is read by the kernels, not the host;
+ * `batch` is the largest row count the call can see and sizes the launch.
+ * The launches do not depend on the row count, so a caller whose mix of
+ * requests changes every step (a continuous-batching loop) can replay the
+ * step from a CUDA graph. */
+bpd_status bpd_soft_step_greedy_from_n(
+    const void* src, int32_t src_dtype, int64_t src_stride, const int64_t* src_rows,
+    float* out, int64_t out_stride, int32_t batch, const int32_t* batch_dev,
+    int32_t vocab_size, int32_t* state_pool, const int64_t* slots,
+    const float* lookahead, const uint32_t* allow_bits, int32_t words_stride,
+    const int32_t* tok_next, int32_t num_states, float alpha, int64_t* token_out,
+    int32_t* next_out, int32_t chunks_per_row, void* step_scratch, void* stream);
+
 /* --------------------------------------------------------------------------
  * Pushdown automaton (context-free grammars)/* --------------------------------------------------------------------------
  * Pushdown automaton (context-free grammars)
@@ -321,6 +335,53 @@ bpd_status bpd_pda_step_greedy_from(
     int32_t* config_pool, const int64_t* slots, uint8_t* broken, int32_t batch,
     void* memo, int32_t memo_capacity, void* workspace, float neg_inf,
     int64_t* token_out, int32_t* status_out, int32_t chunks_per_row, void* stream);
+
+/* NEW: bpd_pda_step_greedy_from over the first *batch_dev rows only (int32
+ * in device memory, read by the kernels; `batch` bounds it and sizes the
+ * launches and the workspace), as bpd_soft_step_greedy_from_n. */
+bpd_status bpd_pda_step_greedy_from_n(
+    const bpd_pda_grammar* g, const void* src, int32_t src_dtype,
+    int64_t src_stride, const int64_t* src_rows, float* out, int64_t out_stride,
+    int32_t* config_pool, const int64_t* slots, uint8_t* broken, int32_t batch,
+    const int32_t* batch_dev, void* memo, int32_t memo_capacity, void* workspace,
+    float neg_inf, int64_t* token_out, int32_t* status_out, int32_t chunks_per_row,
+    void* stream);
+
+/* --------------------------------------------------------------------------
+ * Continuous-batching turnover on the device (NEW; the reference leaves the
+ * serving loop to its callers, vllm.py:100-184). A loop of `rows` rows holds
+ * one request per row: kind[row] 0 = a dense-grammar request (DFA state in
+ * state_pool[row]), 1 = a PDA request (config_pool[row], broken[row]); row r
+ * uses slot r of both pools. dense_rows / pda_rows (int64 [rows]) list the
+ * rows of each kind in ascending order, counts (int32 [2]) their lengths --
+ * the row lists and device row counts of the *_from_n steps.
+ * ------------------------------------------------------------------------ */
+
+/* Retire and admit requests: row r retires with probability evict_prob, drawn
+ * from a counter-based hash of (seed, *step_counter, r) (uint64 counter in
+ * device memory, advanced by one per call). A retired row's new request is a
+ * regex (dense grammar uniform in [0, n_regex)) with probability p_regex, the
+ * dense grammar schema_grammar (-1: none) with probability p_schema, else a
+ * PDA request; its state starts at dense_starts[grammar] (int32, device), or
+ * its config-set at pda_init (int32 [BPD_PDA_CONFIG_INTS], device) with
+ * broken cleared (a PDA row's dense state becomes FREE, -2). retired (uint8
+ * [rows]) records which rows turned over; the row lists and counts are
+ * rebuilt. One CTA; any `rows`. */
+bpd_status bpd_serving_turnover(
+    int32_t rows, uint64_t seed, uint64_t* step_counter, float evict_prob,
+    float p_regex, float p_schema, int32_t n_regex, int32_t schema_grammar,
+    const int32_t* dense_starts, const int32_t* pda_init, int32_t* kind,
+    int32_t* state_pool, int32_t* config_pool, uint8_t* broken,
+    int64_t* dense_rows, int64_t* pda_rows, int32_t* counts, uint8_t* retired,
+    void* stream);
+
+/* tokens_out[dense_rows[b]] = dense_tok[b] for b < counts[0] and
+ * tokens_out[pda_rows[b]] = pda_tok[b] for b < counts[1]: the two steps'
+ * tokens back in row order (int64). */
+bpd_status bpd_serving_gather_tokens(
+    int32_t rows, const int64_t* dense_rows, const int64_t* pda_rows,
+    const int32_t* counts, const int64_t* dense_tok, const int64_t* pda_tok,
+    int64_t* tokens_out, void* stream);
 
 /* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64)./* Advance config-set pool[slots[b]] in place by tokens[b] (int32 or int64).
  * ok_out[b] (uint8, may be NULL) = 1 if the token was accepted; a rejected

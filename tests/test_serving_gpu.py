@@ -71,3 +71,121 @@ def test_admitted_rows_start_fresh() -> None:
             slot = loop.pda._slot_of[q]
             assert torch.equal(loop.pda._configs[slot], init)
             assert not bool(loop.pda._broken[slot])
+
+
+def _host_pda(vocab):
+    import numpy as np
+
+    from bpdecode_b200 import tables
+    from oracle.oracle import HostPda
+
+    arrays = tables.load_pda("jsonvalue")
+    offs = np.zeros(vocab.size + 1, np.int32)
+    np.cumsum([len(t) for t in vocab.token_bytes], out=offs[1:])
+    return HostPda(arrays, offs, np.frombuffer(b"".join(vocab.token_bytes), np.uint8),
+                   vocab.eos_id)
+
+
+def test_device_loop_matches_oracle() -> None:
+    """The device-turnover loop: before every step the row lists and counts
+    match the kinds; every row's token and next state equal the C oracle's
+    from that row's state (soft bias on fp32 working values for dense rows,
+    bounded PDA for grammar rows, broken rows fully masked); after every
+    turnover the retired rows start fresh and the others are untouched."""
+    import numpy as np
+
+    from bpdecode_b200.serving import DeviceServingLoop
+    from bpdecode_b200.workloads import DENSE_PATTERNS
+    from oracle.oracle import Oracle
+
+    orc = Oracle()
+    dense, pda, vocab = _grammars(4096)
+    rows, steps = 160, 48
+    loop = DeviceServingLoop(rows, dense, pda, n_regex=len(DENSE_PATTERNS), seed=21)
+    tn = loop.dense._t.tok_next.cpu().numpy()
+    la = loop.dense._t.lookahead.cpu().numpy()
+    starts = set(loop.dense._t.starts)
+    init = pda.init_config().cpu().numpy()
+    hg = _host_pda(vocab)
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    turned = 0
+    for step in range(steps):
+        logits = (torch.randn(rows, vocab.size, generator=gen, device="cuda") * 2).to(
+            torch.bfloat16)
+        kind = loop.kind.cpu().numpy()
+        pool, cfgs, broken = (x.cpu().numpy().copy() for x in loop.states())
+        d, p = np.flatnonzero(kind == 0), np.flatnonzero(kind == 1)
+        assert loop.counts.cpu().tolist() == [len(d), len(p)], step
+        assert np.array_equal(loop.dense_rows.cpu().numpy()[:len(d)], d), step
+        assert np.array_equal(loop.pda_rows.cpu().numpy()[:len(p)], p), step
+        tok = loop.step(logits).cpu().numpy()
+        work = logits.float().cpu().numpy()
+        wd = np.ascontiguousarray(work[d])
+        orc.apply_soft(wd, la, pool[d], 1.0)
+        want_d = np.argmax(wd, axis=1)
+        next_d = orc.dense_advance(tn, pool[d], want_d)
+        wp = np.ascontiguousarray(work[p])
+        c = np.ascontiguousarray(cfgs[p])
+        orc.pda_apply_mask(hg, c, wp, float("-inf"))
+        br = broken[p].astype(bool)
+        wp[br] = float("-inf")
+        want_p = np.argmax(wp, axis=1)
+        ok = orc.pda_advance(hg, c, want_p)
+        assert np.array_equal(tok[d], want_d), step
+        assert np.array_equal(tok[p], want_p), step
+        pool2, cfgs2, broken2 = (x.cpu().numpy().copy() for x in loop.states())
+        assert np.array_equal(pool2[d], next_d), step
+        assert np.array_equal(cfgs2[p], c), step
+        assert np.array_equal(broken2[p].astype(bool), br | (ok == 0)), step
+        loop.turnover()
+        out = loop.retired.cpu().numpy().astype(bool)
+        turned += int(out.sum())
+        kind3 = loop.kind.cpu().numpy()
+        pool3, cfgs3, broken3 = (x.cpu().numpy() for x in loop.states())
+        keep = ~out
+        assert np.array_equal(kind3[keep], kind[keep]), step
+        assert np.array_equal(pool3[keep], pool2[keep]), step
+        assert np.array_equal(cfgs3[keep], cfgs2[keep]), step
+        for r in np.flatnonzero(out):
+            if kind3[r] == 0:
+                assert int(pool3[r]) in starts, (step, r)
+            else:
+                assert pool3[r] == -2 and not broken3[r], (step, r)
+                assert np.array_equal(cfgs3[r], init), (step, r)
+    # about 10 % of the rows turn over per step
+    assert 0.06 * rows * steps < turned < 0.14 * rows * steps, turned
+
+
+def test_device_loop_graph_replay_equals_eager() -> None:
+    """The same loop replayed from CUDA graphs (one per input buffer, step +
+    turnover captured together) makes the eager loop's decisions."""
+    from bpdecode_b200.serving import DeviceServingLoop
+    from bpdecode_b200.workloads import DENSE_PATTERNS
+
+    dense, pda, vocab = _grammars(4096)
+    rows = 128
+    eager, replay = (DeviceServingLoop(rows, dense, pda, n_regex=len(DENSE_PATTERNS), seed=3)
+                     for _ in range(2))
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    src = [(torch.randn(rows, vocab.size, generator=gen, device="cuda") * 2).to(torch.bfloat16)
+           for _ in range(8)]
+    bufs = [torch.empty_like(src[0]) for _ in range(2)]
+    # one eager step each before capturing (loads the kernels)
+    for lp in (eager, replay):
+        bufs[0].copy_(src[0])
+        lp.step(bufs[0])
+        lp.turnover()
+    graphs = [replay.graph(b) for b in bufs]
+    for step in range(1, 24):
+        b = bufs[step % 2]
+        b.copy_(src[step % 8])
+        ta = eager.step(b).clone()
+        eager.turnover()
+        b.copy_(src[step % 8])
+        graphs[step % 2].replay()
+        assert torch.equal(replay.tokens, ta), step
+        for x, y in zip(eager.states(), replay.states()):
+            assert torch.equal(x, y), step
+        assert torch.equal(eager.kind, replay.kind), step
+        assert torch.equal(eager.counts, replay.counts), step
+    del graphs
