@@ -437,6 +437,27 @@ def run_profile_case(args: argparse.Namespace) -> None:
         batch.reset_many(ids)  # the captured steps start an episode, as in the bench
         for i in range(args.steps):
             step(i)
+    elif args.profile_case == "dense3":
+        # config 3: the schema DFA at V = 151,936, 512 fp32 rows, the
+        # _dense_config3 leg's first buffer copied into the step's input
+        from bpdecode_b200 import tables
+        from bpdecode_b200.batch import ConstraintBatch
+        from bpdecode_b200.ops import FsaTensors
+        from bpdecode_b200.workloads import vocab_large
+
+        B3, V3 = 512, 151_936
+        fsa = FsaTensors.from_arrays(tables.load_dfa("schema"), vocab_large(V3)).to(device)
+        batch = ConstraintBatch(fsa, capacity=B3)
+        ids = list(range(B3))
+        for i in ids:
+            batch.add(i)
+        src = [torch.randn(B3, V3, device=device,
+                           generator=torch.Generator(device=device).manual_seed(7 + i))
+               for i in range(4)]
+        work = torch.empty_like(src[0])
+        for i in range(n):
+            work.copy_(src[i % 4])
+            batch.step_greedy(ids, work)
     elif args.profile_case == "pda_misses":
         from bpdecode_b200 import tables
         from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
@@ -497,7 +518,7 @@ def main() -> None:
                          "batching: regex + schema + GBNF rows, soft lookahead, 10%% turnover)")
     ap.add_argument("--leg", choices=["pda_misses", "pda_config4"],
                     help="run one side measurement alone on cuda:0 and print it")
-    ap.add_argument("--profile-case", choices=["dense", "pda", "soft", "pda_misses"],
+    ap.add_argument("--profile-case", choices=["dense", "dense3", "pda", "soft", "pda_misses"],
                     help="run a few untimed steps of one hot kernel for an ncu capture "
                          "(1 GPU, --warmup steps then --steps steps) and exit")
     args = ap.parse_args()
@@ -584,16 +605,14 @@ def main() -> None:
     torch.cuda.synchronize()
     del busy
     per_launch_ms = [a.elapsed_time(b) for a, b in pairs]
-    kern_ms = statistics.fmean(per_launch_ms)
+    events_ms = statistics.fmean(per_launch_ms)
     rank_ms = shard.gather_over_ranks(elapsed_ms, device)
-    elapsed_ms, kern_ms = shard.max_over_ranks([elapsed_ms, kern_ms], device)
+    elapsed_ms, events_ms = shard.max_over_ranks([elapsed_ms, events_ms], device)
     ms_per_step = elapsed_ms / args.steps
-    # one launch per step, so a kernel cannot take longer than a step (the
-    # tolerance covers the event records' own cost)
-    if kern_ms > ms_per_step * 1.02:
-        raise RuntimeError(f"kernel time {kern_ms:.4f} ms exceeds the step time "
-                           f"{ms_per_step:.4f} ms: the per-launch events are not timing "
-                           "the kernel")
+    # the timed region holds the step kernel's launches back to back and one
+    # index_copy per generation, so its time per step bounds the kernel's own
+    # duration from above (launch gaps included); the roofline uses it
+    kern_ms = ms_per_step
 
     total_rows = ROWS_PER_GPU * world * args.steps
     value = total_rows / (elapsed_ms / 1000.0)
@@ -657,11 +676,17 @@ def main() -> None:
                      "kernel": "stream_step_kernel<bf16, DenseRows, DenseCommit> (fused "
                                "mask + argmax + commit)",
                      "kernel_ms": kern_ms,
-                     "kernel_ms_first_last": [per_launch_ms[0], per_launch_ms[-1]],
-                     "kernel_timing": f"CUDA events around each of the {args.steps} launches "
-                                      "of a replay of the timed steps (same trajectory), the "
-                                      "GPU kept busy by a 1 GiB fill while the first launches "
-                                      "were issued; mean per launch, max over ranks",
+                     "kernel_timing": "the timed region's device time per step (back-to-back "
+                                      "launches of the step kernel, the only kernel there but "
+                                      "one index_copy per generation), max over ranks: an upper "
+                                      "bound of the kernel's duration",
+                     "kernel_ms_events": events_ms,
+                     "kernel_ms_events_first_last": [per_launch_ms[0], per_launch_ms[-1]],
+                     "kernel_events_timing": f"diagnostic: CUDA events around each of the "
+                                             f"{args.steps} launches of a replay of the timed "
+                                             "steps, the GPU kept busy by a 1 GiB fill while the "
+                                             "first launches were issued (each pair adds the "
+                                             "event records' own cost)",
                      "algo_bytes_per_row_step": ALGO_BYTES_PER_ROW_STEP,
                      "algo_bytes_per_launch": ROWS_PER_GPU * ALGO_BYTES_PER_ROW_STEP},
         "clocks": clocks.summary(),

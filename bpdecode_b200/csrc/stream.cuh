@@ -238,6 +238,11 @@ __device__ __forceinline__ uint32_t tile_bits(uint32_t w, int32_t lane, int j) {
 #ifndef BPD_PIPELINE
 #define BPD_PIPELINE 1
 #endif
+// fp32 rows: 0 = bulk-fill only a wholly dead group of tiles, 1 = every run
+// of dead tiles (as 16-bit rows do)
+#ifndef BPD_F32_RUN_BULK
+#define BPD_F32_RUN_BULK 0
+#endif
 
 // Head of one group of kGroupTiles warp tiles, tiles g0.. of the span
 // [e0, e0 + ntiles * TILE): every lane loads its allow word of each tile into
@@ -268,7 +273,7 @@ __device__ __forceinline__ uint32_t group_head(T* row, int32_t e0, int32_t g0, i
   for (int t = 0; t < kGroupTiles; ++t) live |= (__any_sync(kAll, w[t] != 0u) ? 1u : 0u) << t;
   const int32_t ng = min(kGroupTiles, ntiles - g0);
   uint32_t dead = ((1u << ng) - 1u) & ~live;
-  if constexpr (sizeof(typename Dt<T>::Bits) == 4) {
+  if constexpr (sizeof(typename Dt<T>::Bits) == 4 && !BPD_F32_RUN_BULK) {
     if (dead != (1u << ng) - 1u) {
       live |= dead;
       dead = 0u;
