@@ -878,24 +878,8 @@ __device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work
 // Row -> its allow words through the memo / workspace (nullptr for broken rows).
 struct PdaRows {
   static constexpr bool kSoft = false;
-  struct Pre {
-    int32_t kind, ref;
-  };
   Memo memo;
   Work w;
-  __device__ __forceinline__ Pre pre(int32_t row) const { return Pre{w.kind[row], w.ref[row]}; }
-  __device__ __forceinline__ RowInfo info(int32_t row, const Pre& p) const {
-    const uint32_t* b = nullptr;
-    if (p.kind == kHit) {
-      b = memo.bits + static_cast<int64_t>(p.ref) * memo.ws;
-    } else if (p.kind == kRep) {
-      b = (memo.cap && p.ref >= 0) ? memo.bits + static_cast<int64_t>(p.ref) * memo.ws
-                                   : w.bits + static_cast<int64_t>(row) * memo.ws;
-    } else if (p.kind == kAlias) {
-      b = rep_bits(memo, w, p.ref);
-    }
-    return RowInfo{b, 0, 0};
-  }
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {
     return RowInfo{row_bits(memo, w, row), 0, 0};
   }

@@ -109,7 +109,6 @@ __global__ void lookahead_out_kernel(const int32_t* __restrict__ tn, int32_t S, 
 // live) and its lookahead row (the biases); no state = everything -inf.
 struct SoftRows {
   static constexpr bool kSoft = true;
-  using Pre = StatePre;
   const int32_t* pool;
   const int64_t* slots;
   const uint32_t* bits;
@@ -118,16 +117,6 @@ struct SoftRows {
   int32_t S;
   int32_t V;
   float alpha;
-  __device__ __forceinline__ Pre pre(int32_t row) const { return state_pre(pool, slots, row); }
-  __device__ __forceinline__ RowInfo info(int32_t, const Pre& p) const {
-    RowInfo r;
-    r.state = p.state;
-    r.slot = p.slot;
-    const bool ok = p.state >= 0 && p.state < S;
-    r.brow = ok ? bits + static_cast<int64_t>(p.state) * wstride : nullptr;
-    r.lrow = ok ? la + static_cast<int64_t>(p.state) * V : nullptr;
-    return r;
-  }
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {
     RowInfo r;
     r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);

@@ -7,7 +7,6 @@
 // mixed -> load, blend, store.
 #pragma once
 
-#include <algorithm>
 #include <climits>
 #include <type_traits>
 
@@ -238,61 +237,6 @@ __device__ __forceinline__ uint32_t tile_bits(uint32_t w, int32_t lane, int j) {
 #ifndef BPD_PIPELINE
 #define BPD_PIPELINE 1
 #endif
-// fp32 rows: 0 = bulk-fill only a wholly dead group of tiles, 1 = every run
-// of dead tiles (as 16-bit rows do)
-#ifndef BPD_F32_RUN_BULK
-#define BPD_F32_RUN_BULK 0
-#endif
-
-// Head of one group of kGroupTiles warp tiles, tiles g0.. of the span
-// [e0, e0 + ntiles * TILE): every lane loads its allow word of each tile into
-// w (independent loads, one latency for the group), one vote per tile finds
-// the tiles with no allowed token, and lane 0 writes each run of them with
-// the bulk-copy engine from the fill buffer (`issued` tells the caller to
-// wait for the engine before the warp exits). fp32 rows bulk-fill only a
-// wholly dead group; their dead tiles among live ones take plain stores with
-// the live tiles (-4 % on the PDA step, neutral on the soft step; 16-bit rows
-// keep every dead tile on the bulk engine, which is faster there). Returns
-// the mask of the group's tiles left for the vector path.
-template <typename T>
-__device__ __forceinline__ uint32_t group_head(T* row, int32_t e0, int32_t g0, int32_t ntiles,
-                                               const uint32_t* __restrict__ brow,
-                                               const uint4* sfill, uint32_t (&w)[kGroupTiles],
-                                               int32_t lane, int32_t& fill_first,
-                                               bool& issued) {
-  constexpr int TILE = tile_elems<T>();
-  constexpr int WPT = TILE / 32;  // allow words per warp tile
-#pragma unroll
-  for (int t = 0; t < kGroupTiles; ++t) {
-    w[t] = 0u;
-    if (brow != nullptr && g0 + t < ntiles && lane < WPT)
-      w[t] = __ldg(brow + ((e0 + (g0 + t) * TILE) >> 5) + lane);
-  }
-  uint32_t live = 0u;
-#pragma unroll
-  for (int t = 0; t < kGroupTiles; ++t) live |= (__any_sync(kAll, w[t] != 0u) ? 1u : 0u) << t;
-  const int32_t ng = min(kGroupTiles, ntiles - g0);
-  uint32_t dead = ((1u << ng) - 1u) & ~live;
-  if constexpr (sizeof(typename Dt<T>::Bits) == 4 && !BPD_F32_RUN_BULK) {
-    if (dead != (1u << ng) - 1u) {
-      live |= dead;
-      dead = 0u;
-    }
-  }
-  if (dead != 0u && lane == 0) {
-    fill_first = min(fill_first, e0 + (g0 + __ffs(dead) - 1) * TILE);
-    uint32_t d = row != nullptr ? dead : 0u;
-    while (d != 0u) {
-      const int t0 = __ffs(d) - 1;
-      const int run = __ffs(~(d >> t0)) - 1;
-      bulk_fill(row + e0 + (g0 + t0) * TILE,
-                static_cast<uint32_t>(run * TILE * static_cast<int32_t>(sizeof(T))), sfill);
-      d &= ~(((1u << run) - 1u) << t0);
-    }
-    issued = issued || row != nullptr;
-  }
-  return live;
-}
 
 // One warp masks [e0, e1) of `row` (e0 a multiple of the warp tile, so allow
 // words line up) against allow row `brow` (nullptr = reject everything); no
@@ -340,6 +284,7 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
   using Bits = typename Dt<T>::Bits;
   constexpr int EPV = Dt<T>::kPerVec;
   constexpr int TILE = tile_elems<T>();
+  constexpr int WPT = TILE / 32;  // allow words per warp tile
   constexpr uint32_t FULL = (1u << EPV) - 1u;
   const int32_t lane = threadIdx.x & 31;
   int32_t fill_first = INT_MAX;  // lowest index this lane wrote `fill` to
@@ -348,8 +293,40 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
     const int32_t ntiles = nt;
     for (int32_t g0 = 0; g0 < ntiles; g0 += kGroupTiles) {
       uint32_t w[kGroupTiles];
-      const uint32_t live = group_head<T>(row, e0, g0, ntiles, brow, sfill, w, lane, fill_first,
-                                          issued);
+#pragma unroll
+      for (int t = 0; t < kGroupTiles; ++t) {
+        w[t] = 0u;
+        if (brow != nullptr && g0 + t < ntiles && lane < WPT)
+          w[t] = __ldg(brow + ((e0 + (g0 + t) * TILE) >> 5) + lane);
+      }
+      uint32_t live = 0u;
+#pragma unroll
+      for (int t = 0; t < kGroupTiles; ++t)
+        live |= (__any_sync(kAll, w[t] != 0u) ? 1u : 0u) << t;
+      const int32_t ng = min(kGroupTiles, ntiles - g0);
+      uint32_t dead = ((1u << ng) - 1u) & ~live;
+      if constexpr (sizeof(Bits) == 4) {
+        // fp32: only a whole dead group goes out as one bulk store; dead
+        // tiles among live ones take plain stores with them (-4 % on the
+        // PDA step, neutral on the soft step; 16-bit rows keep every dead
+        // tile on the bulk engine, which is faster there)
+        if (dead != (1u << ng) - 1u) {
+          live |= dead;
+          dead = 0u;
+        }
+      }
+      if (dead != 0u && lane == 0) {
+        fill_first = min(fill_first, e0 + (g0 + __ffs(dead) - 1) * TILE);
+        uint32_t d = row != nullptr ? dead : 0u;
+        while (d != 0u) {
+          const int t0 = __ffs(d) - 1;
+          const int run = __ffs(~(d >> t0)) - 1;
+          bulk_fill(row + e0 + (g0 + t0) * TILE,
+                    static_cast<uint32_t>(run * TILE * static_cast<int32_t>(sizeof(T))), sfill);
+          d &= ~(((1u << run) - 1u) << t0);
+        }
+        issued = issued || row != nullptr;
+      }
       if constexpr (!kSoft && BPD_PIPELINE) {
         // Software-pipelined live tiles: while tile t is blended, stored and
         // (with the argmax) folded vector by vector, the loads of tile t + 1
@@ -496,134 +473,6 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
   }
 }
 
-#ifndef BPD_STAGED
-#define BPD_STAGED 1
-#endif
-
-// Shared memory each warp of a staged kernel holds for its group of tiles.
-constexpr int32_t kStageWarpBytes = kGroupTiles * 32 * kVPT * 16;
-constexpr int32_t kStageBytes = kWarps * kStageWarpBytes;
-
-// Per-thread asynchronous 16-byte copy global -> shared (L1 bypassed), and
-// its group bookkeeping: the copies a thread issued before a commit form one
-// group; wait_group<N> returns once at most N of the thread's groups are
-// still in flight.
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(gptr) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-// wait_group with a count known after unrolling (the switch folds away).
-__device__ __forceinline__ void cp_async_wait_n(int n) {
-  static_assert(kGroupTiles <= 4, "cp_async_wait_n covers counts 0..3");
-  switch (n) {
-    case 0: cp_async_wait<0>(); break;
-    case 1: cp_async_wait<1>(); break;
-    case 2: cp_async_wait<2>(); break;
-    default: cp_async_wait<3>(); break;
-  }
-}
-
-// warp_span for an in-place mask of 16-byte aligned rows (no soft bias), with
-// the live tiles of a group staged through shared memory instead of
-// registers: after the group head, every lane issues one asynchronous
-// 16-byte copy per vector that holds an allowed token (per vector the
-// argmax or the blend needs, as in warp_span) for ALL the group's live tiles
-// at once -- one commit group per tile -- so a warp keeps up to kGroupTiles
-// tiles (8 KB) of loads in flight without holding them in registers. It
-// then takes the tiles in order as their groups land: each lane reads back
-// only the vectors it copied itself (its own cp.async.wait_group orders
-// them), blends, stores the changed vectors and folds the argmax, exactly
-// as warp_span does. A stage slot is refilled only by the next group, whose
-// copies are issued after this group's values were consumed by stores and
-// folds that depend on them. `stage` is this warp's kStageWarpBytes.
-template <typename T, bool kArgmax>
-__device__ __forceinline__ void warp_span_staged(T* __restrict__ row, int32_t e0, int32_t nt,
-                                                 int32_t s0, int32_t s1,
-                                                 const uint32_t* __restrict__ brow,
-                                                 typename Dt<T>::Bits fill, const uint4* sfill,
-                                                 uint4* stage, ArgState& st, bool& issued) {
-  using Bits = typename Dt<T>::Bits;
-  constexpr int EPV = Dt<T>::kPerVec;
-  constexpr int TILE = tile_elems<T>();
-  constexpr int VPT = 32 * kVPT;  // 16-byte vectors per warp tile
-  constexpr uint32_t FULL = (1u << EPV) - 1u;
-  static_assert(EPV * kVPT <= 32, "a tile's bits of one lane fit one word");
-  const int32_t lane = threadIdx.x & 31;
-  int32_t fill_first = INT_MAX;
-  VecArg va;
-  const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
-  for (int32_t g0 = 0; g0 < nt; g0 += kGroupTiles) {
-    uint32_t w[kGroupTiles];
-    const uint32_t live = group_head<T>(row, e0, g0, nt, brow, sfill, w, lane, fill_first,
-                                        issued);
-    // this lane's bits of its kVPT vectors of each tile, packed EPV bits each
-    uint32_t lb[kGroupTiles];
-#pragma unroll
-    for (int t = 0; t < kGroupTiles; ++t) {
-      lb[t] = 0u;
-#pragma unroll
-      for (int j = 0; j < kVPT; ++j) lb[t] |= tile_bits<T>(w[t], lane, j) << (j * EPV);
-    }
-#pragma unroll
-    for (int t = 0; t < kGroupTiles; ++t) {
-      if ((live >> t) & 1u) {
-        const T* tp = row + e0 + (g0 + t) * TILE;
-#pragma unroll
-        for (int j = 0; j < kVPT; ++j) {
-          const uint32_t b = (lb[t] >> (j * EPV)) & FULL;
-          const bool need = kArgmax ? (b != 0u) : (b != 0u && b != FULL);
-          const int v = lane + 32 * j;
-          if (need) cp_async16(sbase + static_cast<uint32_t>((t * VPT + v) * 16), tp + v * EPV);
-        }
-      }
-      cp_async_commit();
-    }
-#pragma unroll
-    for (int t = 0; t < kGroupTiles; ++t) {
-      cp_async_wait_n(kGroupTiles - 1 - t);
-      if (((live >> t) & 1u) == 0u) continue;
-      const int32_t tb = e0 + (g0 + t) * TILE;
-      uint4* base = reinterpret_cast<uint4*>(row + tb);
-#pragma unroll
-      for (int j = 0; j < kVPT; ++j) {
-        const uint32_t b = (lb[t] >> (j * EPV)) & FULL;
-        const bool need = kArgmax ? (b != 0u) : (b != 0u && b != FULL);
-        const int v = lane + 32 * j;
-        uint4 val = make_uint4(0u, 0u, 0u, 0u);
-        if (need) val = stage[t * VPT + v];
-        const uint4 out = vec_blend<T>(val, b, fill);
-        if (b != FULL) __stcs(base + v, out);
-        if constexpr (kArgmax) vec_arg_fold(va, vec_max<T>(out), tb + v * EPV);
-      }
-    }
-  }
-  if (issued) asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-  Bits* rb = reinterpret_cast<Bits*>(row);
-  for (int32_t e = s0 + lane; e < s1; e += 32) {
-    const bool allowed = brow != nullptr && ((__ldg(brow + (e >> 5)) >> (e & 31)) & 1u);
-    if (allowed) {
-      if constexpr (kArgmax) arg_elem(st, Dt<T>::to_float(rb[e]), e);
-    } else {
-      rb[e] = fill;
-      fill_first = min(fill_first, e);
-    }
-  }
-  if constexpr (kArgmax) {
-    if (va.vec != INT_MAX) {
-      // the winning vector, read back from the row (every lane's own stores
-      // and the untouched all-allowed vectors)
-      vec_arg_resolve<T>(st, va, *reinterpret_cast<const uint4*>(row + va.vec));
-    }
-    if (fill_first != INT_MAX) arg_elem(st, Dt<T>::to_float(fill), fill_first);
-  }
-}
-
 // ---------------------------------------------------------------------------
 // Kernels built on warp_span, shared by the dense, soft and PDA paths. A CTA
 // owns `chunk` elements of one row (kWarps equal spans, one per warp); the
@@ -664,40 +513,13 @@ __device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__
   return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
 }
 
-// A Rows functor gives a row's RowInfo in two steps, so that a persistent
-// warp can issue the loads for its next row while it streams the current
-// one: pre(row) only loads (its results are consumed later), info(row, pre)
-// does the arithmetic. operator()(row) is both at once.
-struct StatePre {
-  int64_t slot;
-  int32_t state;
-};
-
-__device__ __forceinline__ StatePre state_pre(const int32_t* __restrict__ pool,
-                                              const int64_t* __restrict__ slots, int32_t row) {
-  StatePre p;
-  p.slot = slots ? slots[row] : row;
-  p.state = pool[p.slot];
-  return p;
-}
-
 struct DenseRows {
   static constexpr bool kSoft = false;
-  using Pre = StatePre;
   const int32_t* pool;
   const int64_t* slots;
   const uint32_t* bits;
   int32_t wstride;
   int32_t S;
-  __device__ __forceinline__ Pre pre(int32_t row) const { return state_pre(pool, slots, row); }
-  __device__ __forceinline__ RowInfo info(int32_t, const Pre& p) const {
-    RowInfo r;
-    r.state = p.state;
-    r.slot = p.slot;
-    r.brow = (p.state >= 0 && p.state < S) ? bits + static_cast<int64_t>(p.state) * wstride
-                                           : nullptr;
-    return r;
-  }
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {
     RowInfo r;
     r.brow = state_row(pool, slots, row, bits, wstride, S, &r.state, &r.slot);
@@ -747,27 +569,6 @@ struct DenseCommit {
 #ifndef BPD_TILES_PER_WARP
 #define BPD_TILES_PER_WARP 4
 #endif
-// Resident CTAs per SM of the staged kernels (shared memory bound: the fill
-// buffer and 64 KB of stage per CTA).
-#ifndef BPD_STAGED_MIN_BLOCKS
-#define BPD_STAGED_MIN_BLOCKS 3
-#endif
-
-// Whether a streaming kernel instantiation stages its live tiles through
-// shared memory (warp_span_staged): the in-place mask without soft bias.
-template <bool kVec, bool kInPlace, class Rows>
-constexpr bool staged_path() {
-  return BPD_STAGED != 0 && kVec && kInPlace && !Rows::kSoft;
-}
-
-// Dynamic shared memory of a streaming CTA: the fill buffer, the stage of a
-// staged kernel, then the commit's own bytes.
-template <bool kStaged>
-constexpr size_t stream_smem_bytes(size_t commit_bytes) {
-  // staged: the committing warp's stage slice holds the commit's bytes
-  return static_cast<size_t>(kFillBytes) +
-         (kStaged ? static_cast<size_t>(kStageBytes) : commit_bytes);
-}
 
 // Chunk of one CTA: `chunks_per_row` CTAs per row when the caller asks for
 // it, else BPD_TILES_PER_WARP warp tiles per warp. Always a multiple of
@@ -825,9 +626,7 @@ __device__ __forceinline__ WarpShare warp_share(int32_t c0, int32_t c1) {
 
 // Mask only: one CTA per (row, chunk).
 template <typename T, bool kVec, class Rows>
-__global__ void __launch_bounds__(kThreads, staged_path<kVec, true, Rows>()
-                                                ? BPD_STAGED_MIN_BLOCKS
-                                                : BPD_APPLY_MIN_BLOCKS)
+__global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
     stream_apply_kernel(T* __restrict__ logits, int64_t row_stride, int32_t V, Rows rows,
                         typename Dt<T>::Bits fill, int32_t chunk, int32_t chunks_per_row) {
   extern __shared__ __align__(16) uint8_t smem[];
@@ -842,44 +641,33 @@ __global__ void __launch_bounds__(kThreads, staged_path<kVec, true, Rows>()
   ArgState st;
   bool issued = false;
   T* rowp = logits + row * row_stride;
-  if constexpr (staged_path<kVec, true, Rows>()) {
-    uint4* stage = reinterpret_cast<uint4*>(smem + kFillBytes +
-                                            (threadIdx.x >> 5) * kStageWarpBytes);
-    warp_span_staged<T, false>(rowp, ws.e0, ws.nt, ws.s0, ws.s1, info.brow, fill,
-                               reinterpret_cast<const uint4*>(smem), stage, st, issued);
-  } else {
-    warp_span<T, T, true, kVec, false, Rows::kSoft>(rowp, rowp, ws.e0, ws.nt, ws.s0,
-                                                    ws.s1, info.brow, fill,
-                                                    reinterpret_cast<const uint4*>(smem),
-                                                    info.lrow, rows_alpha(rows), st, issued);
-  }
+  warp_span<T, T, true, kVec, false, Rows::kSoft>(rowp, rowp, ws.e0, ws.nt, ws.s0,
+                                                  ws.s1, info.brow, fill,
+                                                  reinterpret_cast<const uint4*>(smem), info.lrow,
+                                                  rows_alpha(rows), st, issued);
   if (issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 // Device scratch of the fused step: per row the best packed (key, ~index) so
-// far and the number of pieces done, and the persistent kernel's work queue
-// (next item, warps finished). It must be zero before a launch; every launch
-// that runs to completion leaves it zero again (the row's last piece clears
-// the row's words, the last warp out clears the queue).
+// far and the number of warps done. It must be zero before a launch; every
+// launch that runs to completion leaves it zero again (the row's last warp
+// clears it).
 struct StepScratch {
   unsigned long long* best;  // [batch]
   uint32_t* done;            // [batch]
-  uint32_t* queue;           // [2]
 };
 
 constexpr size_t step_scratch_bytes(int32_t batch) {
   return align256(sizeof(unsigned long long) * static_cast<size_t>(batch)) +
-         align256(sizeof(uint32_t) * static_cast<size_t>(batch)) + 256;
+         align256(sizeof(uint32_t) * static_cast<size_t>(batch));
 }
 
 inline StepScratch step_scratch_view(void* base, int32_t batch) {
   char* p = static_cast<char*>(base);
   StepScratch s;
   s.best = reinterpret_cast<unsigned long long*>(p);
-  p += align256(sizeof(unsigned long long) * static_cast<size_t>(batch));
-  s.done = reinterpret_cast<uint32_t*>(p);
-  p += align256(sizeof(uint32_t) * static_cast<size_t>(batch));
-  s.queue = reinterpret_cast<uint32_t*>(p);
+  s.done = reinterpret_cast<uint32_t*>(
+      p + align256(sizeof(unsigned long long) * static_cast<size_t>(batch)));
   return s;
 }
 
@@ -896,9 +684,7 @@ inline StepScratch step_scratch_view(void* base, int32_t batch) {
 // T), or nowhere when `logits` is nullptr.
 template <typename T, typename S, bool kInPlace, bool kVec, class Rows, class Commit>
 __global__ void __launch_bounds__(kThreads,
-                                  Rows::kSoft ? BPD_SOFT_STEP_MIN_BLOCKS
-                                  : staged_path<kVec, kInPlace, Rows>() ? BPD_STAGED_MIN_BLOCKS
-                                                                         : BPD_STEP_MIN_BLOCKS)
+                                  Rows::kSoft ? BPD_SOFT_STEP_MIN_BLOCKS : BPD_STEP_MIN_BLOCKS)
     stream_step_kernel(T* __restrict__ logits, int64_t row_stride, const S* __restrict__ src,
                        int64_t src_stride, const int64_t* __restrict__ src_rows, int32_t V,
                        Rows rows, Commit commit, typename Dt<T>::Bits fill, int32_t chunk,
@@ -907,8 +693,11 @@ __global__ void __launch_bounds__(kThreads,
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ unsigned long long warp_q[kWarps];
   __shared__ uint32_t warps_done;
-  // rows at or past a device-held row count are not part of this call
-  if (nrows != nullptr && static_cast<int32_t>(blockIdx.x / chunks_per_row) >= *nrows) return;
+  // rows at or past a device-held row count are not part of this call (the
+  // *_from_n entry points; the in-place steps never take one)
+  if constexpr (!kInPlace) {
+    if (nrows != nullptr && static_cast<int32_t>(blockIdx.x / chunks_per_row) >= *nrows) return;
+  }
   if (threadIdx.x == 0) warps_done = 0u;
   if constexpr (kVec) fill_init<T>(smem, fill);
   __syncthreads();
@@ -925,20 +714,10 @@ __global__ void __launch_bounds__(kThreads,
   } else {
     srow = src + (src_rows != nullptr ? src_rows[row] : static_cast<int64_t>(row)) * src_stride;
   }
-  constexpr bool kStaged = staged_path<kVec, kInPlace, Rows>();
-  static_assert(!kStaged || Commit::kSmemBytes <= kStageWarpBytes,
-                "a commit fits one warp's stage slice");
-  if constexpr (kStaged) {
-    uint4* stage = reinterpret_cast<uint4*>(smem + kFillBytes +
-                                            (threadIdx.x >> 5) * kStageWarpBytes);
-    warp_span_staged<T, true>(rowp, sh.e0, sh.nt, sh.s0, sh.s1, info.brow, fill,
-                              reinterpret_cast<const uint4*>(smem), stage, st, issued);
-  } else {
-    warp_span<T, S, kInPlace, kVec, true, Rows::kSoft>(rowp, srow, sh.e0, sh.nt, sh.s0,
-                                                       sh.s1, info.brow, fill,
-                                                       reinterpret_cast<const uint4*>(smem),
-                                                       info.lrow, rows_alpha(rows), st, issued);
-  }
+  warp_span<T, S, kInPlace, kVec, true, Rows::kSoft>(rowp, srow, sh.e0, sh.nt, sh.s0,
+                                                     sh.s1, info.brow, fill,
+                                                     reinterpret_cast<const uint4*>(smem),
+                                                     info.lrow, rows_alpha(rows), st, issued);
   // Two-level last-arriver merge, no barrier: the CTA's last warp (a shared
   // memory count) merges the CTA's 8 partials and takes part in the row's
   // count in global memory; the row's last CTA commits.
@@ -977,212 +756,7 @@ __global__ void __launch_bounds__(kThreads,
     if (issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
   }
   tok = __shfl_sync(kAll, tok, 0);
-  // the commit's shared memory: after the fill buffer, or -- staged -- this
-  // warp's own stage slice, whose loads were all consumed by its span
-  uint8_t* csmem = kStaged ? smem + kFillBytes + (threadIdx.x >> 5) * kStageWarpBytes
-                           : smem + kFillBytes;
-  if (tok >= 0) commit(row, info, tok, csmem);
-}
-
-// Lets `kernel` use `bytes` of dynamic shared memory on the current device
-// (needed above 48 KB); done once per kernel and device.
-template <auto kernel>
-bpd_status allow_smem(size_t bytes, const char* what) {
-  if (bytes <= 48 * 1024) return BPD_OK;
-  constexpr int kMaxDev = 64;
-  static int done[kMaxDev] = {};  // 1 + the size set, per device
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev)
-    return fail(BPD_ERR_CUDA, "%s: cannot query the current device", what);
-  if (done[dev] == static_cast<int>(bytes) + 1) return BPD_OK;
-  const cudaError_t e = cudaFuncSetAttribute(
-      kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e != cudaSuccess)
-    return fail(BPD_ERR_CUDA, "%s: shared memory size %zu: %s", what, bytes,
-                cudaGetErrorString(e));
-  done[dev] = static_cast<int>(bytes) + 1;
-  return BPD_OK;
-}
-
-// ---------------------------------------------------------------------------
-// Persistent fused step: a grid of resident CTAs whose WARPS take work items
-// -- (row, segment of seg_tiles warp tiles) -- from an atomic queue. The CTA
-// fills its shared fill buffer once for the whole launch; each warp fetches
-// its next item index one item ahead and issues the loads of that item's
-// row (Rows::pre) before it streams the current one, so the dependent chain
-// of a row (slot -> state -> allow row) overlaps the streaming instead of
-// preceding it. A row's pieces meet as in stream_step_kernel: one 64-bit
-// atomicMax per piece and an acquire-release count; the warp that completes
-// the row commits it. Nothing waits on another warp or CTA; the last warp to
-// finish resets the queue (release fence before each warp's exit count).
-//
-// The last segment of a row also takes its ragged end (V mod TILE elements,
-// one per lane). Segments past the row's tiles (chunks_per_row larger than
-// the tile count) are empty pieces that still count.
-#ifndef BPD_PERSIST
-#define BPD_PERSIST 1
-#endif
-#ifndef BPD_PERSIST_BLOCKS
-#define BPD_PERSIST_BLOCKS 5
-#endif
-#ifndef BPD_SEG_TILES
-#define BPD_SEG_TILES 8
-#endif
-
-template <typename T, typename S, bool kInPlace, class Rows, class Commit>
-__global__ void __launch_bounds__(kThreads, BPD_PERSIST_BLOCKS)
-    persist_step_kernel(T* __restrict__ logits, int64_t row_stride, const S* __restrict__ src,
-                        int64_t src_stride, const int64_t* __restrict__ src_rows, int32_t V,
-                        Rows rows, Commit commit, typename Dt<T>::Bits fill, int32_t seg_tiles,
-                        int32_t segs_per_row, int32_t items, StepScratch ws,
-                        const int32_t* __restrict__ nrows) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int32_t TILE = tile_elems<T>();
-  fill_init<T>(smem, fill);
-  __syncthreads();
-  const uint4* sfill = reinterpret_cast<const uint4*>(smem);
-  const int32_t lane = threadIdx.x & 31;
-  uint8_t* csmem = smem + kFillBytes + (threadIdx.x >> 5) * Commit::kSmemBytes;
-  const int32_t ntr = V / TILE;  // full warp tiles of a row
-  uint32_t item = 0, nxt = 0;
-  if (lane == 0) {
-    item = atomicAdd(ws.queue, 1u);
-    nxt = atomicAdd(ws.queue, 1u);
-  }
-  item = __shfl_sync(kAll, item, 0);
-  nxt = __shfl_sync(kAll, nxt, 0);
-  // with a device-held row count, only the items of rows below it
-  const uint32_t nitems =
-      nrows == nullptr
-          ? static_cast<uint32_t>(items)
-          : static_cast<uint32_t>(min(items, max(0, min(*nrows, items / segs_per_row)) *
-                                                 segs_per_row));
-  typename Rows::Pre pre{};
-  if (item < nitems) pre = rows.pre(static_cast<int32_t>(item) / segs_per_row);
-  bool any_issued = false;
-  while (item < nitems) {
-    const int32_t row = static_cast<int32_t>(item) / segs_per_row;
-    const int32_t seg = static_cast<int32_t>(item) - row * segs_per_row;
-    // the next item's row loads and the index after it: in flight while
-    // this item streams
-    typename Rows::Pre npre{};
-    if (nxt < nitems) npre = rows.pre(static_cast<int32_t>(nxt) / segs_per_row);
-    uint32_t after = 0;
-    if (lane == 0 && nxt < nitems) after = atomicAdd(ws.queue, 1u);
-    const RowInfo info = rows.info(row, pre);
-    const int32_t t0 = seg * seg_tiles;
-    const int32_t nt = max(0, min(seg_tiles, ntr - t0));
-    const bool last = seg == segs_per_row - 1;
-    const int32_t e0 = min(t0, ntr) * TILE;
-    const int32_t s0 = ntr * TILE;
-    const int32_t s1 = last ? V : s0;
-    T* rowp = logits != nullptr ? logits + row * row_stride : nullptr;
-    const S* srow;
-    if constexpr (kInPlace) {
-      srow = rowp;
-    } else {
-      srow = src + (src_rows != nullptr ? src_rows[row] : static_cast<int64_t>(row)) * src_stride;
-    }
-    ArgState st;
-    bool issued = false;
-    warp_span<T, S, kInPlace, true, true, Rows::kSoft>(rowp, srow, e0, nt, s0, s1, info.brow,
-                                                        fill, sfill, info.lrow, rows_alpha(rows),
-                                                        st, issued);
-    any_issued = any_issued || issued;
-    const unsigned long long q = warp_max_u64(pack_arg(st.key, st.idx));
-    int32_t tok = -1;
-    if (lane == 0) {
-      if (segs_per_row == 1) {
-        tok = unpack_idx(q);
-      } else {
-        atomicMax(ws.best + row, q);
-        uint32_t arrived;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                     : "=r"(arrived)
-                     : "l"(ws.done + row)
-                     : "memory");
-        if (arrived == static_cast<uint32_t>(segs_per_row - 1)) {
-          const unsigned long long b = atomicExch(ws.best + row, 0ull);
-          ws.done[row] = 0u;
-          tok = unpack_idx(b);
-        }
-      }
-      // bound the bulk stores this thread has in flight (their source is the
-      // read-only fill buffer, so only the count matters)
-      if (any_issued) asm volatile("cp.async.bulk.wait_group.read 8;" ::: "memory");
-    }
-    tok = __shfl_sync(kAll, tok, 0);
-    if (tok >= 0) commit(row, info, tok, csmem);
-    item = nxt;
-    nxt = __shfl_sync(kAll, after, 0);
-    pre = npre;
-  }
-  if (lane == 0) {
-    if (any_issued) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-    // every queue fetch of this warp is ordered before its exit count; the
-    // last warp out sees all of them and clears the queue for the next launch
-    __threadfence();
-    uint32_t out;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
-                 : "=r"(out)
-                 : "l"(ws.queue + 1)
-                 : "memory");
-    if (out == gridDim.x * static_cast<uint32_t>(kWarps) - 1u) {
-      ws.queue[0] = 0u;
-      ws.queue[1] = 0u;
-    }
-  }
-}
-
-// Work layout of the persistent step: warp tiles per segment and segments
-// per row. chunks_per_row > 0 sets the segment count; 0 picks BPD_SEG_TILES
-// tiles per segment, halved for small batches until there are about 4 items
-// per SM.
-struct PersistLayout {
-  int32_t seg_tiles, segs, items, grid;
-};
-
-template <typename T>
-inline PersistLayout persist_layout(int32_t V, int32_t batch, int32_t chunks_per_row) {
-  constexpr int32_t TILE = tile_elems<T>();
-  const int32_t ntr = V / TILE;
-  const int64_t sms = sm_count();
-  PersistLayout L;
-  if (chunks_per_row > 0) {
-    L.segs = chunks_per_row;
-    L.seg_tiles = max(1, (ntr + L.segs - 1) / L.segs);
-  } else {
-    L.seg_tiles = BPD_SEG_TILES;
-    while (L.seg_tiles > 1 &&
-           static_cast<int64_t>(batch) * ((ntr + L.seg_tiles - 1) / L.seg_tiles) < sms * 4)
-      L.seg_tiles /= 2;
-    L.segs = max(1, (ntr + L.seg_tiles - 1) / L.seg_tiles);
-  }
-  const int64_t items = static_cast<int64_t>(batch) * L.segs;
-  L.items = items < 0x7FFFFFFF ? static_cast<int32_t>(items) : -1;
-  L.grid = static_cast<int32_t>(std::min<int64_t>(sms * BPD_PERSIST_BLOCKS, std::max<int64_t>(items, 1)));
-  return L;
-}
-
-template <typename T, typename S, bool kInPlace, class Rows, class Commit>
-bpd_status launch_persist_step(T* out, int64_t out_stride, const S* src, int64_t src_stride,
-                               const int64_t* src_rows, int32_t batch, int32_t V,
-                               const Rows& rows, const Commit& commit,
-                               typename Dt<T>::Bits fill, int32_t chunks_per_row,
-                               const StepScratch& ws, cudaStream_t st, const char* what,
-                               const int32_t* nrows = nullptr) {
-  const PersistLayout L = persist_layout<T>(V, batch, chunks_per_row);
-  if (L.items < 0) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
-  const size_t smem = static_cast<size_t>(kFillBytes) +
-                      static_cast<size_t>(kWarps) * static_cast<size_t>(Commit::kSmemBytes);
-  const bpd_status rc =
-      allow_smem<persist_step_kernel<T, S, kInPlace, Rows, Commit>>(smem, what);
-  if (rc) return rc;
-  persist_step_kernel<T, S, kInPlace, Rows, Commit>
-      <<<static_cast<unsigned>(L.grid), kThreads, smem, st>>>(
-          out, out_stride, src, src_stride, src_rows, V, rows, commit, fill, L.seg_tiles, L.segs,
-          L.items, ws, nrows);
-  return check_launch(what);
+  if (tok >= 0) commit(row, info, tok, smem + kFillBytes);
 }
 
 inline bool rows_aligned(const void* logits, int64_t row_stride, size_t esize) {
@@ -1206,10 +780,7 @@ bpd_status launch_stream_apply(void* logits, int64_t row_stride, int32_t batch, 
   const auto fill = Dt<T>::from_float_host(neg_inf);
   T* lg = static_cast<T*>(logits);
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    constexpr size_t smem = stream_smem_bytes<staged_path<true, true, Rows>()>(0);
-    const bpd_status rc = allow_smem<stream_apply_kernel<T, true, Rows>>(smem, what);
-    if (rc) return rc;
-    stream_apply_kernel<T, true, Rows><<<static_cast<unsigned>(grid), kThreads, smem, st>>>(
+    stream_apply_kernel<T, true, Rows><<<static_cast<unsigned>(grid), kThreads, kFillBytes, st>>>(
         lg, row_stride, V, rows, fill, chunk, chunks);
   } else {
     stream_apply_kernel<T, false, Rows><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
@@ -1234,21 +805,11 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   const StepScratch ws = step_scratch_view(scratch, batch);
   T* lg = static_cast<T*>(logits);
   const size_t smem = kFillBytes + Commit::kSmemBytes;
-  if (BPD_PERSIST && vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    return launch_persist_step<T, T, true, Rows, Commit>(lg, row_stride, lg, row_stride, nullptr,
-                                                         batch, V, rows, commit, fill,
-                                                         chunks_per_row, ws, st, what);
-  }
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    constexpr size_t vsmem =
-        stream_smem_bytes<staged_path<true, true, Rows>()>(Commit::kSmemBytes);
-    const bpd_status rc =
-        allow_smem<stream_step_kernel<T, T, true, true, Rows, Commit>>(vsmem, what);
-    if (rc) return rc;
     stream_step_kernel<T, T, true, true, Rows, Commit>
-        <<<static_cast<unsigned>(grid), kThreads, vsmem, st>>>(lg, row_stride, lg, row_stride,
-                                                                nullptr, V, rows, commit, fill,
-                                                                chunk, cpr, ws, nullptr);
+        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(lg, row_stride, lg, row_stride,
+                                                               nullptr, V, rows, commit, fill,
+                                                               chunk, cpr, ws, nullptr);
   } else {
     stream_step_kernel<T, T, true, false, Rows, Commit>
         <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(lg, row_stride, lg, row_stride,
@@ -1281,12 +842,6 @@ bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int
                    (out == nullptr || rows_aligned(out, out_stride, sizeof(float))) &&
                    (!Rows::kSoft || V % 4 == 0);
   const S* sp = static_cast<const S*>(src);
-  if (BPD_PERSIST && vec) {
-    return launch_persist_step<float, S, false, Rows, Commit>(out, out_stride, sp, src_stride,
-                                                              src_rows, batch, V, rows, commit,
-                                                              fill, chunks_per_row, ws, st, what,
-                                                              nrows);
-  }
   if (vec) {
     stream_step_kernel<float, S, false, true, Rows, Commit>
         <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(out, out_stride, sp, src_stride,
