@@ -87,6 +87,19 @@ def _profile_traffic(steps: int) -> tuple[float | None, str]:
         f"steps {min(want)}..{max(want)} (the steps this run timed), profiles/dense_step_config2.md")
 
 
+def _profile_bytes(name: str) -> float | None:
+    """`traffic_bytes_per_launch: <bytes>` of a committed ncu summary under
+    profiles/ (DRAM read + write per launch of that leg's kernel), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML while running."""
 
@@ -820,6 +833,9 @@ def _pda_config4(device: torch.device, rank: int, steps: int = 512) -> dict:
             "first_step_us_cold_memo": first,
             "unfused_us_median": {k: sorted(v)[len(v) // 2] for k, v in part.items()},
             "row_steps_per_s": B / (us[len(us) // 2] * 1e-6), "broken_rows_at_end": broken,
+            "step_kernel_traffic_bytes": _profile_bytes("pda_step_config4.md"),
+            "traffic_source": "ncu DRAM bytes per launch of the PDA step kernel, "
+                              "profiles/pda_step_config4.md",
             "note": "the bounded PDA saturates at init on this grammar (8 configs), as the "
                     "reference does; after the first steps every row's config-set hits the memo"}
 
@@ -937,11 +953,18 @@ def _dense_config3(device: torch.device, rank: int, steps: int = 256) -> dict:
     algo = 2 * V3 * 4 + 4 * ((V3 + 31) // 32) + 16
     peak, _ = _peaks()
     achieved = B3 * algo / (mean * 1e-6) / 1e9
+    traffic = _profile_bytes("dense_step_config3.md")
     return {"workload": "JSON-Schema object as a dense DFA (1017 states), V=151936, 512 rows, "
                         "fp32 N(0,1), greedy, 256 steps from the start state",
             "us_per_step": mean, "row_steps_per_s": B3 / (mean * 1e-6),
             "algo_bytes_per_row_step": algo, "achieved_gbs": achieved,
-            "roofline_frac": achieved / peak}
+            "roofline_frac": achieved / peak,
+            "traffic_bytes_per_launch": traffic,
+            "traffic_gbs": traffic / (mean * 1e-6) / 1e9 if traffic else None,
+            "roofline_frac_traffic": traffic / (mean * 1e-6) / 1e9 / peak if traffic else None,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch, "
+                              "profiles/dense_step_config3.md (rejected vectors are written "
+                              "without being read, so the algorithmic fraction exceeds 1)"}
 
 
 def _soft_lookahead(fsas, pats, device: torch.device, rank: int, steps: int = 128) -> dict:
