@@ -861,7 +861,8 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2)
     rule NFAs, not the dense DFA), 256 rows, V = 128,256, fp32 N(0, 1), greedy;
     the memo and the transition cache are cleared at the start of each
     32-step generation. Per step: device time (CUDA events around
-    CFGConstraintBatch.step_greedy, issued eagerly) and the number of distinct
+    CFGConstraintBatch.step_greedy, issued eagerly behind the step's input
+    copy, as in _pda_config4) and the number of distinct
     config-sets the rows hold that the generation had not seen before (read
     between steps, untimed)."""
     from bpdecode_b200 import tables
@@ -884,8 +885,6 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2)
         batch.step_greedy(ids, work)
     us: list[list[float]] = []
     new: list[list[int]] = []
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
     for gen in range(gens):
         g.clear_memo()
         for r in ids:
@@ -894,15 +893,18 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2)
         us.append([])
         new.append([])
         for step in range(steps):
-            rows = set(_canon_rows(batch._configs.cpu().numpy()))
+            rows = set(_canon_rows(batch._configs.cpu().numpy()))  # synchronises
             new[-1].append(len(rows - seen))
             seen |= rows
+            # the input copy (131 MB) keeps the GPU busy while the step's
+            # launches are issued, so the events time the step's kernels
             work.copy_(src[(gen * steps + step) % ring])
-            torch.cuda.synchronize()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
             a.record()
             batch.step_greedy(ids, work)
             b.record()
-            torch.cuda.synchronize()
+            b.synchronize()
             us[-1].append(a.elapsed_time(b) * 1000)
     flat = [x for u in us for x in u]
     miss = [x for u, n in zip(us, new) for x, k in zip(u, n) if k > 0]

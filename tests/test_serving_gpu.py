@@ -189,3 +189,44 @@ def test_device_loop_graph_replay_equals_eager() -> None:
         assert torch.equal(eager.kind, replay.kind), step
         assert torch.equal(eager.counts, replay.counts), step
     del graphs
+
+
+def test_device_turnover_lists_over_many_rows() -> None:
+    """The device turnover over 2500 rows (three blocks of the kernel's
+    1024-row compaction): after every call the ascending row lists and their
+    counts match the kinds, retired rows hold fresh states, the others keep
+    theirs, and the retirement rate is about the configured fraction."""
+    import numpy as np
+
+    from bpdecode_b200.serving import DeviceServingLoop
+    from bpdecode_b200.workloads import DENSE_PATTERNS
+
+    dense, pda, _ = _grammars(1024)
+    rows = 2500
+    loop = DeviceServingLoop(rows, dense, pda, n_regex=len(DENSE_PATTERNS), seed=17,
+                             evict_fraction=0.25)
+    starts = set(loop.dense._t.starts)
+    init = pda.init_config().cpu().numpy()
+    turned = 0
+    for _ in range(6):
+        kind0 = loop.kind.cpu().numpy()
+        pool0 = loop.dense._state.cpu().numpy().copy()
+        loop.turnover()
+        kind = loop.kind.cpu().numpy()
+        out = loop.retired.cpu().numpy().astype(bool)
+        turned += int(out.sum())
+        d, p = np.flatnonzero(kind == 0), np.flatnonzero(kind == 1)
+        assert len(d) + len(p) == rows
+        assert loop.counts.cpu().tolist() == [len(d), len(p)]
+        assert np.array_equal(loop.dense_rows.cpu().numpy()[:len(d)], d)
+        assert np.array_equal(loop.pda_rows.cpu().numpy()[:len(p)], p)
+        pool = loop.dense._state.cpu().numpy()
+        cfgs = loop.pda._configs.cpu().numpy()
+        assert np.array_equal(kind[~out], kind0[~out])
+        assert np.array_equal(pool[~out], pool0[~out])
+        assert all(int(pool[r]) in starts for r in np.flatnonzero(out & (kind == 0)))
+        for r in np.flatnonzero(out & (kind == 1))[:50]:
+            assert pool[r] == -2 and np.array_equal(cfgs[r], init)
+    assert 0.20 * rows * 6 < turned < 0.30 * rows * 6, turned
+    # the mix of admitted requests follows (0.5, 0.3, 0.2): dense about 80 %
+    assert 0.72 < float((loop.kind == 0).float().mean()) < 0.88
