@@ -551,6 +551,8 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
                                            int32_t* B) {
   const int lane = threadIdx.x & 31;
   const int64_t slot = slot_of(slots, b);
+  // this call's tag, loaded beside the row (it does not depend on it)
+  const uint32_t epoch = memo.cap ? *memo.epoch : 0u;
   const bool brk = broken != nullptr && broken[slot] != 0;
   w_load_row(pool + slot * NCFG, A, lane);
   if (brk) {
@@ -564,7 +566,7 @@ __device__ __forceinline__ void lookup_row(const bpd_pda_grammar& g,
   int32_t kind = kRep, ref = -1;
   uint32_t cur = 0;  // this call's tag
   if (memo.cap) {
-    cur = *memo.epoch + 1u;
+    cur = epoch + 1u;
     if (cur == 0u) cur = 1u;
   }
   // memo: entries claimed earlier in this call (tag == cur) are still being
