@@ -471,12 +471,15 @@ def run_profile_case(args: argparse.Namespace) -> None:
         for i in range(n):
             work.copy_(src[i % 4])
             batch.step_greedy(ids, work)
-    elif args.profile_case == "pda_misses":
+    elif args.profile_case in ("pda_misses", "pda_nesting"):
         from bpdecode_b200 import tables
         from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
-        from bpdecode_b200.workloads import vocab_large
+        from bpdecode_b200.workloads import BIASED, vocab_large
 
-        g = PdaTensors.from_arrays(tables.load_pda("schema"), vocab_large(V), device)
+        nest = args.profile_case == "pda_nesting"
+        vocab = vocab_large(V)
+        g = PdaTensors.from_arrays(tables.load_pda("brackets" if nest else "schema"), vocab,
+                                   device)
         batch = CFGConstraintBatch(g, capacity=256)
         ids = list(range(256))
         for i in ids:
@@ -484,6 +487,10 @@ def run_profile_case(args: argparse.Namespace) -> None:
         src = [torch.randn(256, V, device=device,
                            generator=torch.Generator(device=device).manual_seed(500 + i))
                for i in range(4)]
+        if nest:
+            boost = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
+            for x in src:
+                x[:, boost] += 1.0
         work = torch.empty_like(src[0])
         g.clear_memo()
         for i in range(n):
@@ -529,9 +536,10 @@ def main() -> None:
     ap.add_argument("--workload", default="config2", choices=["config2", "config5"],
                     help="config2 (default, the headline line) or config5 (whole-box continuous "
                          "batching: regex + schema + GBNF rows, soft lookahead, 10%% turnover)")
-    ap.add_argument("--leg", choices=["pda_misses", "pda_config4"],
+    ap.add_argument("--leg", choices=["pda_misses", "pda_nesting", "pda_config4"],
                     help="run one side measurement alone on cuda:0 and print it")
-    ap.add_argument("--profile-case", choices=["dense", "dense3", "pda", "soft", "pda_misses"],
+    ap.add_argument("--profile-case",
+                    choices=["dense", "dense3", "pda", "soft", "pda_misses", "pda_nesting"],
                     help="run a few untimed steps of one hot kernel for an ncu capture "
                          "(1 GPU, --warmup steps then --steps steps) and exit")
     args = ap.parse_args()
@@ -543,7 +551,8 @@ def main() -> None:
     if args.leg:
         dev = torch.device("cuda", 0)
         torch.cuda.set_device(dev)
-        fn = {"pda_misses": _pda_misses, "pda_config4": _pda_config4}[args.leg]
+        fn = {"pda_misses": _pda_misses, "pda_nesting": _pda_nesting,
+              "pda_config4": _pda_config4}[args.leg]
         print(json.dumps({args.leg: fn(dev, 0)}), flush=True)
         return
     if args.workload == "config5" and args.impl == "ours":
@@ -717,6 +726,7 @@ def main() -> None:
         torch.cuda.empty_cache()
         line["pda_config4"] = _pda_config4(device, rank)
         line["pda_misses"] = _pda_misses(device, rank)
+        line["pda_nesting"] = _pda_nesting(device, rank)
         line["dense_config3"] = _dense_config3(device, rank)
         line["soft_lookahead"] = _soft_lookahead(fsas, pats, device, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -855,7 +865,16 @@ def _canon_rows(cfg) -> list[bytes]:
     return out
 
 
-def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2) -> dict:
+def _pda_nesting(device: torch.device, rank: int) -> dict:
+    """The PDA path where nearly every row meets a config-set no row held
+    before at every step: root ::= item+, item ::= "(" item* ")" | "[" item*
+    "]" | "x" (the stack records the open brackets), 256 rows, V = 128,256,
+    fp32 N(0, 1) + 1 on the { [ " , tokens; otherwise as _pda_misses."""
+    return _pda_misses(device, rank, name="brackets", bias=1.0)
+
+
+def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2,
+                name: str = "schema", bias: float = 0.0) -> dict:
     """The PDA path on a grammar that keeps producing config-sets the memo
     has not seen: the JSON-Schema object of config 3 as a PDA (its 1354-state
     rule NFAs, not the dense DFA), 256 rows, V = 128,256, fp32 N(0, 1), greedy;
@@ -869,8 +888,11 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2)
     from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
     from bpdecode_b200.workloads import vocab_large
 
+    from bpdecode_b200.workloads import BIASED
+
     B = 256
-    g = PdaTensors.from_arrays(tables.load_pda("schema"), vocab_large(V), device)
+    vocab = vocab_large(V)
+    g = PdaTensors.from_arrays(tables.load_pda(name), vocab, device)
     batch = CFGConstraintBatch(g, capacity=B)
     ids = list(range(B))
     for i in ids:
@@ -879,6 +901,10 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2)
     src = [torch.randn(B, V, device=device,
                        generator=torch.Generator(device=device).manual_seed(rank * 97 + 500 + i))
            for i in range(ring)]
+    if bias:
+        boost = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
+        for x in src:
+            x[:, boost] += bias
     work = torch.empty_like(src[0])
     for i in range(2):  # load the kernels, allocate the memo and workspace
         work.copy_(src[i])
@@ -908,9 +934,15 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2)
             us[-1].append(a.elapsed_time(b) * 1000)
     flat = [x for u in us for x in u]
     miss = [x for u, n in zip(us, new) for x, k in zip(u, n) if k > 0]
-    return {"workload": "JSON-Schema object as a PDA (1354 states), 256 rows, V=128256, fp32 "
-                        f"N(0,1), greedy, {gens} generations of {steps} steps, memo and "
+    what = {"schema": "JSON-Schema object as a PDA (1354 states)",
+            "brackets": 'root ::= item+, item ::= "(" item* ")" | "[" item* "]" | "x" as a PDA'}
+    return {"workload": f"{what.get(name, name)}, 256 rows, V=128256, fp32 N(0,1)"
+                        + (f" + {bias:g} on the {{ [ \" , tokens" if bias else "")
+                        + f", greedy, {gens} generations of {steps} steps, memo and "
                         "transition cache cleared at the start of each",
+            "rows_per_step": B,
+            "new_sets_share_late_mean": statistics.fmean(
+                k / B for n in new for k in n[steps // 2:]),
             "step": "CFGConstraintBatch.step_greedy, eager",
             "us_per_step_mean": statistics.fmean(flat),
             "us_per_step_with_new_sets_mean": statistics.fmean(miss) if miss else None,

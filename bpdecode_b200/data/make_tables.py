@@ -43,6 +43,12 @@ PDA_TEST_GRAMMARS = {
     "xy": 'root ::= "x" | "y"',
 }
 
+# A grammar whose stack records the sequence of open brackets, so greedy rows
+# keep reaching config-sets no row held before (the PDA memo-miss workload).
+MISS_GRAMMARS = {
+    "brackets": 'root ::= item+\nitem ::= "(" item* ")" | "[" item* "]" | "x"',
+}
+
 
 def _dfa_arrays(prefix: str, dfa, out: dict) -> None:
     from bpdecode.fsa import fsa_from_dfa
@@ -95,7 +101,7 @@ def main() -> None:
                 CompiledGrammar.build(parse_gbnf(_PRIMITIVES + "\nroot ::= json-value\n")), out)
     _pda_arrays("pda/schema", schema_cg, out)
     _pda_arrays("pda/hf_object", CompiledGrammar.build(json_schema_to_grammar(HF_SCHEMA)), out)
-    for name, src in PDA_TEST_GRAMMARS.items():
+    for name, src in {**PDA_TEST_GRAMMARS, **MISS_GRAMMARS}.items():
         _pda_arrays(f"pda/{name}", CompiledGrammar.build(parse_gbnf(src)), out)
 
     np.savez_compressed(OUT, **out)

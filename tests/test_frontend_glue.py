@@ -33,13 +33,14 @@ def _grammars():
     from bpdecode.grammar.json_schema import _PRIMITIVES, json_schema_to_grammar
     from bpdecode.grammar.pda import CompiledGrammar
 
-    from bpdecode_b200.data.make_tables import HF_SCHEMA, PDA_TEST_GRAMMARS
+    from bpdecode_b200.data.make_tables import HF_SCHEMA, MISS_GRAMMARS, PDA_TEST_GRAMMARS
     from bpdecode_b200.workloads import SCHEMA_OBJECT
 
     out = [("jsonvalue", CompiledGrammar.build(parse_gbnf(_PRIMITIVES + "\nroot ::= json-value\n"))),
            ("schema", CompiledGrammar.build(json_schema_to_grammar(SCHEMA_OBJECT))),
            ("hf_object", CompiledGrammar.build(json_schema_to_grammar(HF_SCHEMA)))]
-    out += [(n, CompiledGrammar.build(parse_gbnf(src))) for n, src in PDA_TEST_GRAMMARS.items()]
+    out += [(n, CompiledGrammar.build(parse_gbnf(src)))
+            for n, src in {**PDA_TEST_GRAMMARS, **MISS_GRAMMARS}.items()]
     return out
 
 

@@ -82,11 +82,14 @@ def _run_against_reference(name: str, V: int, B: int, steps: int, memo_capacity:
 
 
 @pytest.mark.parametrize("memo_capacity", [4096, 16, 1])
-@pytest.mark.parametrize("name", ["schema", "jsonvalue", "pairs", "paren", "hf_object"])
+@pytest.mark.parametrize("name", ["schema", "jsonvalue", "pairs", "paren", "hf_object",
+                                  "brackets"])
 def test_generation_equals_reference_cuda(name: str, memo_capacity: int) -> None:
-    distinct = _run_against_reference(name, 4096, 96, 24, memo_capacity, seed=5,
-                                      bias=2.0 if name in ("paren", "jsonvalue") else 0.0)
+    bias = {"paren": 2.0, "jsonvalue": 2.0, "brackets": 1.0}.get(name, 0.0)
+    distinct = _run_against_reference(name, 4096, 96, 24, memo_capacity, seed=5, bias=bias)
     assert distinct > 1
+    if name == "brackets":
+        assert distinct > 96 * 8  # most rows reach a new config-set every step
 
 
 def test_schema_misses_at_full_vocabulary_equal_reference_cuda() -> None:
@@ -95,6 +98,15 @@ def test_schema_misses_at_full_vocabulary_equal_reference_cuda() -> None:
     start; most steps bring config-sets the memo has not seen."""
     distinct = _run_against_reference("schema", 128_256, 256, 24, 4096, seed=9)
     assert distinct > 24
+
+
+def test_brackets_misses_at_full_vocabulary_equal_reference_cuda() -> None:
+    """The benchmark's nesting leg: root ::= item+, item ::= "(" item* ")" |
+    "[" item* "]" | "x"; the stack records the open brackets, so nearly every
+    row holds a config-set no row held before at every step. 256 rows,
+    V = 128,256, fp32 N(0, 1) + 1 on the { [ " , tokens."""
+    distinct = _run_against_reference("brackets", 128_256, 256, 16, 4096, seed=13, bias=1.0)
+    assert distinct > 256 * 6
 
 
 def test_paren_nesting_walks_equal_reference_cuda() -> None:
