@@ -488,7 +488,9 @@ def run_profile_case(args: argparse.Namespace) -> None:
                            generator=torch.Generator(device=device).manual_seed(500 + i))
                for i in range(4)]
         if nest:
-            boost = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
+            from bpdecode_b200.workloads import OPENERS, token_ids
+
+            boost = torch.tensor(token_ids(vocab, OPENERS), device=device)
             for x in src:
                 x[:, boost] += 1.0
         work = torch.empty_like(src[0])
@@ -869,12 +871,14 @@ def _pda_nesting(device: torch.device, rank: int) -> dict:
     """The PDA path where nearly every row meets a config-set no row held
     before at every step: root ::= item+, item ::= "(" item* ")" | "[" item*
     "]" | "x" (the stack records the open brackets), 256 rows, V = 128,256,
-    fp32 N(0, 1) + 1 on the { [ " , tokens; otherwise as _pda_misses."""
-    return _pda_misses(device, rank, name="brackets", bias=1.0)
+    fp32 N(0, 1) + 1 on the "(" and "[" tokens; otherwise as _pda_misses."""
+    from bpdecode_b200.workloads import OPENERS
+
+    return _pda_misses(device, rank, name="brackets", bias=1.0, boost_tokens=OPENERS)
 
 
 def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2,
-                name: str = "schema", bias: float = 0.0) -> dict:
+                name: str = "schema", bias: float = 0.0, boost_tokens=None) -> dict:
     """The PDA path on a grammar that keeps producing config-sets the memo
     has not seen: the JSON-Schema object of config 3 as a PDA (its 1354-state
     rule NFAs, not the dense DFA), 256 rows, V = 128,256, fp32 N(0, 1), greedy;
@@ -888,7 +892,7 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2,
     from bpdecode_b200.grammar.device import CFGConstraintBatch, PdaTensors
     from bpdecode_b200.workloads import vocab_large
 
-    from bpdecode_b200.workloads import BIASED
+    from bpdecode_b200.workloads import BIASED, token_ids
 
     B = 256
     vocab = vocab_large(V)
@@ -902,7 +906,7 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2,
                        generator=torch.Generator(device=device).manual_seed(rank * 97 + 500 + i))
            for i in range(ring)]
     if bias:
-        boost = torch.tensor([vocab.token_bytes.index(t) for t in BIASED], device=device)
+        boost = torch.tensor(token_ids(vocab, boost_tokens or BIASED), device=device)
         for x in src:
             x[:, boost] += bias
     work = torch.empty_like(src[0])
@@ -937,7 +941,9 @@ def _pda_misses(device: torch.device, rank: int, steps: int = 32, gens: int = 2,
     what = {"schema": "JSON-Schema object as a PDA (1354 states)",
             "brackets": 'root ::= item+, item ::= "(" item* ")" | "[" item* "]" | "x" as a PDA'}
     return {"workload": f"{what.get(name, name)}, 256 rows, V=128256, fp32 N(0,1)"
-                        + (f" + {bias:g} on the {{ [ \" , tokens" if bias else "")
+                        + (f" + {bias:g} on the "
+                           + " ".join(t.decode() for t in (boost_tokens or BIASED))
+                           + " tokens" if bias else "")
                         + f", greedy, {gens} generations of {steps} steps, memo and "
                         "transition cache cleared at the start of each",
             "rows_per_step": B,

@@ -58,6 +58,14 @@ SCHEMA_OBJECT = {
 # Reserved single-byte tokens at ids 0..6 of the large vocabularies.
 RESERVED = (b"{", b"[", b'"', b",", b"}", b"]", b":")
 BIASED = (b"{", b"[", b'"', b",")  # +3 logit bias in the recursive-GBNF config
+OPENERS = (b"(", b"[")  # +1 logit bias in the brackets (memo-miss) workload
+
+
+def token_ids(vocab, tokens) -> list[int]:
+    """Every id whose bytes equal one of `tokens` (a synthetic vocabulary may
+    hold a byte string more than once)."""
+    want = set(tokens)
+    return [i for i, t in enumerate(vocab.token_bytes) if t in want]
 
 _CONFIG1_ALPHABET = b"0123456789.abcdefghijklmnopqrstuvwxyzABCDEFGHIJKLMNOPQRSTUVWXYZ "
 
