@@ -218,11 +218,15 @@ struct Nodes {
   int32_t* trans;            // [ncap][256] 0 unknown, 1 being computed, 2 the set dies,
                              //             3 + id: next node
   int32_t cap;               // power of two, 0 = none
+  uint32_t* full;            // the memo header's "a node could not be interned" flag
 };
 
 struct Memo {
-  uint32_t* epoch;  // [1] calls so far; entries claimed by the running call carry
-                    //     tag epoch + 1 and are skipped by its own lookups
+  uint32_t* epoch;  // header (256 B): [0] calls so far -- entries claimed by the
+                    //     running call carry tag epoch + 1 and are skipped by its
+                    //     own lookups; [1] set when a node could not be interned
+                    //     (the table is full: the next call clears it);
+                    //     [2] the call prologue's finished-CTA count
   uint32_t* tag;    // [cap] 0 = empty, else the claiming call's tag
   uint64_t* hash;   // [cap]
   int32_t* key;     // [cap][NCFG] canonical config-sets
@@ -232,7 +236,10 @@ struct Memo {
   Nodes nodes;      // transition cache (kNodesPerEntry per memo entry)
 };
 
-constexpr int32_t kNodesPerEntry = 4;
+// 16 nodes per memo entry: 64K nodes (~137 MB) at the default 4096 entries,
+// room for a whole call of ~250 new config-sets with their walks' prefixes.
+constexpr int32_t kNodesPerEntry = 16;
+constexpr int kHdrNodesFull = 1, kHdrPrologueDone = 2;
 #ifndef BPD_PDA_NODES
 #define BPD_PDA_NODES 1  // 0: miss path without the transition cache (for comparisons)
 #endif
@@ -258,6 +265,7 @@ Memo memo_view(void* base, int32_t cap, int32_t vocab) {
   p += align256(sizeof(uint32_t) * m.ws * static_cast<size_t>(cap));
   const size_t ncap = static_cast<size_t>(cap) * kNodesPerEntry;
   m.nodes.cap = static_cast<int32_t>(ncap);
+  m.nodes.full = m.epoch + kHdrNodesFull;
   m.nodes.hash = reinterpret_cast<unsigned long long*>(p);
   p += align256(sizeof(unsigned long long) * ncap);
   m.nodes.ready = reinterpret_cast<uint32_t*>(p);
@@ -487,6 +495,7 @@ __device__ int32_t node_intern(const Nodes& nd, const int32_t* c, uint64_t h, in
     }
     if (w_same_words(c, kw, lane)) return e;
   }
+  if (lane == 0) atomicOr(nd.full, 1u);  // the next call starts on an empty table
   return -1;
 }
 
@@ -999,6 +1008,42 @@ __global__ void complete_kernel(bpd_pda_grammar g, const int32_t* __restrict__ p
   out[b] = (!(broken && broken[slot]) && is_complete(g, pool + slot * NCFG)) ? 1 : 0;
 }
 
+// The first launch of every mask call, in place of a memset: zero the call's
+// dedup table, counters and step scratch (Work::clear_bytes from w.dedup)
+// and, when the previous call found the transition cache full (a node it
+// could not intern), the whole node table -- so a grammar whose walks keep
+// reaching new config-sets starts each call with room instead of falling
+// back to direct walks for good. Every CTA reads the flag before it counts
+// itself done, and the last CTA out clears flag and count, so all CTAs act
+// on the same flag value.
+constexpr int kPrologueThreads = 256;
+
+__global__ void __launch_bounds__(kPrologueThreads)
+    prologue_kernel(Memo memo, Work w, size_t node_bytes) {
+  const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  uint4* wz = reinterpret_cast<uint4*>(w.dedup);
+  for (size_t i = tid; i < w.clear_bytes / 16; i += stride) wz[i] = zero;
+  if (memo.cap == 0) return;
+  __shared__ uint32_t full;
+  if (threadIdx.x == 0) full = *reinterpret_cast<volatile uint32_t*>(memo.epoch + kHdrNodesFull);
+  __syncthreads();
+  if (full != 0u && node_bytes != 0) {
+    uint4* nz = reinterpret_cast<uint4*>(memo.nodes.hash);
+    for (size_t i = tid; i < node_bytes / 16; i += stride) nz[i] = zero;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(memo.epoch + kHdrPrologueDone, 1u);
+    if (done == gridDim.x - 1u) {
+      memo.epoch[kHdrNodesFull] = 0u;
+      memo.epoch[kHdrPrologueDone] = 0u;
+    }
+  }
+}
+
 bpd_status check_grammar(const bpd_pda_grammar* g) {
   BPD_REQUIRE(g != nullptr, "null grammar");
   BPD_REQUIRE(g->accept && g->live && g->edge_offsets && g->tok_offsets && g->tok_bytes,
@@ -1022,15 +1067,19 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
   BPD_REQUIRE(pool && workspace, "null config pool or workspace");
   BPD_REQUIRE(memo_mem == nullptr || (cap > 0 && (cap & (cap - 1)) == 0),
               "memo capacity must be a power of two");
+  BPD_REQUIRE(aligned16(workspace) && (memo_mem == nullptr || aligned16(memo_mem)),
+              "workspace and memo must be 16-byte aligned");
   Memo memo = memo_view(memo_mem, cap, g->vocab_size);
   Work w = work_view(workspace, batch, g->vocab_size);
-  cudaError_t e = cudaMemsetAsync(w.dedup, 0, w.clear_bytes, st);
-  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "memset dedup: %s", cudaGetErrorString(e));
+  const int32_t sms = sm_count();
+  prologue_kernel<<<sms, kPrologueThreads, 0, st>>>(
+      memo, w, (BPD_PDA_NODES && memo.nodes.cap > 0) ? nodes_clear_bytes(cap) : 0);
+  rc = check_launch("pda prologue_kernel");
+  if (rc) return rc;
   lookup_kernel<<<(batch + kLookupWarps - 1) / kLookupWarps, kLookupWarps * 32, 0, st>>>(
       *g, pool, slots, broken, batch, memo, w, nrows);
   rc = check_launch("pda lookup_kernel");
   if (rc) return rc;
-  const int32_t sms = sm_count();
   // With a transition cache the compute walks take every token from its
   // first byte through the cache; without one, the first bytes that keep
   // each representative alive are found first, so that tokens starting with

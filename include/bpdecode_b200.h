@@ -282,14 +282,19 @@ bpd_status bpd_pda_init(const bpd_pda_grammar* g, int32_t* config_out, void* str
 /* Mask-memo table in caller-owned device memory (NEW; the per-config mask memo
  * held in HBM). bpd_pda_memo_bytes gives the size for `capacity` entries;
  * bpd_pda_memo_reset clears it (call once after allocating, and to drop every
- * cached mask). capacity must be a power of two. */
+ * cached mask). capacity must be a power of two; the buffer 16-byte aligned.
+ * It also holds the miss path's transition cache (16 config-set nodes per
+ * entry); a call that finds that cache full has the next call start it over.
+ * Calls that share a memo must be ordered on one stream; after a call that
+ * failed on the device, reset the memo before using it again. */
 size_t bpd_pda_memo_bytes(int32_t capacity, int32_t vocab_size);
 bpd_status bpd_pda_memo_reset(void* memo, int32_t capacity, int32_t vocab_size,
                               void* stream);
 
 /* NEW: per-call scratch of bpd_pda_apply_mask / bpd_pda_mask_bits /
  * bpd_pda_step_greedy for `batch` rows (the reference allocates its per-row
- * PdaConfigSet copies in local memory inside its kernels, pda_cuda.cu:40-95). */
+ * PdaConfigSet copies in local memory inside its kernels, pda_cuda.cu:40-95).
+ * 16-byte aligned; any contents (each call clears what it needs). */
 size_t bpd_pda_workspace_bytes(int32_t batch, int32_t vocab_size);
 
 /* Packed allow bits per row, int32 [batch, ceil(vocab/32)], of config-set
