@@ -62,6 +62,8 @@ def _run_against_reference(name: str, V: int, B: int, steps: int, memo_capacity:
     gen = torch.Generator(device="cuda").manual_seed(seed)
     seen: set[bytes] = set()
     ref_broken = torch.zeros(B, dtype=torch.bool, device="cuda")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    ms_mine, ms_ref = [], []
     for step in range(steps):
         for row in batch._configs.cpu().numpy():
             seen.add(row.tobytes())
@@ -69,17 +71,29 @@ def _run_against_reference(name: str, V: int, B: int, steps: int, memo_capacity:
         if bias:
             logits[:, boost] += bias
         mine, want = logits.clone(), logits.clone()
+        ev[0].record()
         tok = batch.step_greedy(ids, mine)
+        ev[1].record()
         # the reference's CFGConstraintBatch step (grammar/device.py:252-283)
+        ev[2].record()
         ref.pda_apply_mask(g, ref_cfg, want)
         want[ref_broken] = float("-inf")
         ref_tok = want.argmax(-1)
         ok = ref.pda_advance(g, ref_cfg, ref_tok.to(torch.int32))
+        ev[3].record()
+        torch.cuda.synchronize()
+        ms_mine.append(ev[0].elapsed_time(ev[1]))
+        ms_ref.append(ev[2].elapsed_time(ev[3]))
         ref_broken |= ok == 0
         assert torch.equal(mine, want), (name, step)
         assert torch.equal(tok, ref_tok), (name, step)
         assert torch.equal(batch._configs, ref_cfg), (name, step)
         assert torch.equal(batch._broken.bool(), ref_broken), (name, step)
+    # printed with -s: this library's fused step against the reference's mask +
+    # argmax + advance on the same rows, ms per step (mean of the second half)
+    h = steps // 2
+    print(f"\n{name} V={V} B={B}: step {sum(ms_mine[h:]) / (steps - h):.3f} ms here, "
+          f"{sum(ms_ref[h:]) / (steps - h):.3f} ms reference CUDA")
     return len(seen)
 
 
