@@ -190,15 +190,38 @@ __device__ __forceinline__ uint64_t l2_evict_last_policy() {
 // Warp tiles whose allow words a warp loads at once.
 constexpr int kGroupTiles = 4;
 
+// Cache policy of the logits stream: 0 = streaming (evict-first) loads and
+// stores, 1 = loads and stores cached at L2 only (.cg).
+#ifndef BPD_STREAM_CG
+#define BPD_STREAM_CG 0
+#endif
+
+template <typename V>
+__device__ __forceinline__ V ld_stream(const V* p) {
+  if constexpr (BPD_STREAM_CG) {
+    return __ldcg(p);
+  } else {
+    return __ldcs(p);
+  }
+}
+
+__device__ __forceinline__ void st_stream(uint4* p, const uint4& v) {
+  if constexpr (BPD_STREAM_CG) {
+    __stcg(p, v);
+  } else {
+    __stcs(p, v);
+  }
+}
+
 // The 16-byte vector of working type T at element e0 of a source row of type
 // S: the same bits when S == T, else (T = float) EPV elements of S widened.
 template <typename T, typename S>
 __device__ __forceinline__ uint4 load_src(const S* __restrict__ srow, int32_t e0) {
   if constexpr (std::is_same_v<S, T>) {
-    return __ldcs(reinterpret_cast<const uint4*>(srow + e0));
+    return ld_stream(reinterpret_cast<const uint4*>(srow + e0));
   } else {
     static_assert(std::is_same_v<T, float> && sizeof(S) == 2, "fp32 from 16-bit sources");
-    const uint2 h = __ldcs(reinterpret_cast<const uint2*>(srow + e0));
+    const uint2 h = ld_stream(reinterpret_cast<const uint2*>(srow + e0));
     if constexpr (std::is_same_v<S, __nv_bfloat16>) {
       return make_uint4(h.x << 16, h.x & 0xFFFF0000u, h.y << 16, h.y & 0xFFFF0000u);
     } else {
@@ -357,7 +380,7 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
           for (int j = 0; j < kVPT; ++j) {
             const uint32_t b = tile_bits<T>(w[t], lane, j);
             const uint4 out = vec_blend<T>(val[j], b, fill);
-            if (row != nullptr && (!kInPlace || b != FULL)) __stcs(base + lane + 32 * j, out);
+            if (row != nullptr && (!kInPlace || b != FULL)) st_stream(base + lane + 32 * j, out);
             if (next) {
               const uint32_t bn = tile_bits<T>(w[t + 1 < kGroupTiles ? t + 1 : t], lane, j);
               const bool need = (kArgmax || !kInPlace) ? (bn != 0u) : (bn != 0u && bn != FULL);
@@ -419,7 +442,7 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
               out = vec_blend<T>(val[jj], bits[j], fill);
             }
             if (row != nullptr && (kSoft || !kInPlace || bits[j] != FULL))
-              __stcs(base + lane + 32 * j, out);
+              st_stream(base + lane + 32 * j, out);
             if constexpr (kArgmax)
               vec_arg_fold(va, vec_max<T>(out), tb + (lane + 32 * j) * EPV);
           }
