@@ -755,21 +755,34 @@ __device__ __forceinline__ void node_walk(const bpd_pda_grammar& g, const Nodes&
 }
 
 constexpr int32_t kComputeChunk = kWarps * 32 * 4;  // tokens per compute item
+constexpr int32_t kPrefillItems = 256 / (kWarps * 4);  // first-byte items per node (4 bytes a warp)
 
-// Allow bits of every representative row. Items are (representative, 1024
-// tokens) pairs taken from a counter by a resident grid; each warp decides 32
-// tokens at a time (lane = token), walking only the ones whose first byte
-// survives and that are longer than one byte.
+// Allow bits of every representative row. Items are taken from a counter by a
+// resident grid: first, per representative with a node, kPrefillItems items
+// that fill the node's 256 first-byte transitions (4 bytes a warp, each one
+// bounded closure unless already known), so a new node's first steps are
+// computed in parallel; then (representative, 1024 tokens) items, each warp
+// deciding 32 tokens at a time (lane = token). With a node, the item's copy of
+// the node's first-byte row in shared memory rejects a token whose first byte
+// kills the set with one shared read and starts a longer token's walk at the
+// node after its first byte; transitions not known when the row was copied
+// go through the table (node_walk). Without a node, only tokens whose first
+// byte survives (first_byte_kernel) and that are longer than one byte are
+// walked directly.
 __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
                                               const int32_t* __restrict__ pool,
                                               const int64_t* __restrict__ slots,
                                               const Memo& memo, const Work& w,
                                               bool first_valid, int32_t (*buf)[2][NCFG],
-                                              uint32_t* first, int32_t& s_item) {
+                                              uint32_t* first, int32_t* strans,
+                                              int32_t& s_item) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int32_t V = g.vocab_size;
   const int32_t chunks = (V + kComputeChunk - 1) / kComputeChunk;
-  const int32_t items = w.counters[0] * chunks;
+  const int32_t reps = w.counters[0];
+  const bool nodes = memo.nodes.cap > 0 && !first_valid;
+  const int32_t prefill = nodes ? reps * kPrefillItems : 0;
+  const int32_t items = prefill + reps * chunks;
   if (items == 0) return;  // the same value for every thread of the CTA
   for (;;) {
     __syncthreads();  // the previous item's shared state is no longer read
@@ -777,21 +790,37 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
     __syncthreads();
     const int32_t item = s_item;
     if (item >= items) break;
-    const int32_t b = w.reps[item / chunks];
-    const int32_t c0 = (item % chunks) * kComputeChunk;
+    if (item < prefill) {
+      // first-byte transitions of a representative's node, 4 bytes a warp
+      const int32_t nd = w.node[w.reps[item / kPrefillItems]];
+      if (nd >= 0) {
+        const int32_t b0 = (item % kPrefillItems) * (kWarps * 4) + warp * 4;
+        for (int k = 0; k < 4; ++k) node_step(g, memo.nodes, nd, b0 + k, buf[warp][0],
+                                              buf[warp][1], lane);
+      }
+      continue;
+    }
+    const int32_t ti = item - prefill;
+    const int32_t b = w.reps[ti / chunks];
+    const int32_t c0 = (ti % chunks) * kComputeChunk;
     const int32_t c1 = min(V, c0 + kComputeChunk);
     const int32_t* base = pool + slot_of(slots, b) * NCFG;
+    const int32_t nd0 = w.node[b];
     if (first_valid && threadIdx.x < 8)
       first[threadIdx.x] = w.first[static_cast<int64_t>(b) * 8 + threadIdx.x];
+    if (nd0 >= 0) {
+      for (int k = threadIdx.x; k < 256; k += blockDim.x)
+        strans[k] = __ldcg(memo.nodes.trans + static_cast<int64_t>(nd0) * 256 + k);
+    }
     __syncthreads();
     const bool eos_ok = w.eos_ok[b] != 0;
     const bool nonempty = n_of(base) > 0;
-    const int32_t nd0 = w.node[b];
     uint32_t* out = rep_bits(memo, w, b);
     for (int32_t t0 = c0 + warp * 32; t0 < c1; t0 += kWarps * 32) {
       const int32_t t = t0 + lane;
       bool ok = false, walk = false;
       int32_t o0 = 0, o1 = 0;
+      int32_t q = nd0;  // the node a lane's walk starts from (with a node)
       if (t < c1) {
         if (t == g.eos_id) {
           ok = eos_ok;
@@ -800,8 +829,24 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
           o1 = __ldg(g.tok_offsets + t + 1);
           if (o0 == o1) {
             ok = nonempty;
-          } else if (nd0 >= 0 || !first_valid) {
-            walk = true;  // through the transition cache, or a direct walk
+          } else if (nd0 >= 0) {
+            // the first byte through the node's row copied above
+            const int32_t v = strans[__ldg(g.tok_bytes + o0)];
+            if (v == kTransDead) {
+              // the set dies on the first byte: rejected
+            } else if (v >= kTransNode && v - kTransNode < memo.nodes.cap) {
+              if (o1 - o0 == 1) {
+                ok = true;
+              } else {
+                q = v - kTransNode;
+                ++o0;
+                walk = true;
+              }
+            } else {
+              walk = true;  // not known when copied: through the table
+            }
+          } else if (!first_valid) {
+            walk = true;  // a direct walk
           } else {
             const int fb = __ldg(g.tok_bytes + o0);
             if ((first[fb >> 5] >> (fb & 31)) & 1u) {
@@ -812,7 +857,7 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
         }
       }
       if (nd0 >= 0) {
-        node_walk(g, memo.nodes, nd0, o0, o1, walk, ok, buf[warp], lane);
+        node_walk(g, memo.nodes, q, o0, o1, walk, ok, buf[warp], lane);
         walk = false;
       }
       uint32_t todo = __ballot_sync(kAll, walk);
@@ -867,8 +912,9 @@ __global__ void __launch_bounds__(kThreads)
                    const int64_t* __restrict__ slots, Memo memo, Work w, int32_t first_valid) {
   __shared__ int32_t buf[kWarps][2][NCFG];
   __shared__ uint32_t first[8];
+  __shared__ int32_t strans[256];
   __shared__ int32_t s_item;
-  compute_items(g, pool, slots, memo, w, first_valid != 0, buf, first, s_item);
+  compute_items(g, pool, slots, memo, w, first_valid != 0, buf, first, strans, s_item);
   // the last kernel of every mask call: the next call gets a new tag (the
   // lookups of this call, which read the old epoch, have all finished)
   if (memo.cap && blockIdx.x == 0 && threadIdx.x == 0) {

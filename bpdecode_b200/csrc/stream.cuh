@@ -191,9 +191,11 @@ __device__ __forceinline__ uint64_t l2_evict_last_policy() {
 constexpr int kGroupTiles = 4;
 
 // Cache policy of the logits stream: 0 = streaming (evict-first) loads and
-// stores, 1 = loads and stores cached at L2 only (.cg).
+// stores, 1 = loads and stores cached at L2 only (.cg). .cg measured 2 %
+// faster on the config-2 step (86.7 against 88.4 µs per step over the first
+// 20 steps of a generation, 65.1 against 66.3 over 128; same-box A/B).
 #ifndef BPD_STREAM_CG
-#define BPD_STREAM_CG 0
+#define BPD_STREAM_CG 1
 #endif
 
 template <typename V>
