@@ -582,11 +582,14 @@ struct DenseCommit {
 // fused dense step -11 % in late steps (the pipelined tile loop), mask-only
 // launches -5 % over a config-2 generation (pipelined too; +11 % on the first
 // step alone), fused soft step -7 % over a generation, soft apply -7 %.
+// The fused (non-soft) step then went to 64 registers (4 CTAs per SM, no
+// spills): -1 % on the config-2 step with the .cg stream (85.8 against
+// 86.8 µs over the first 20 steps of a generation; 6 CTAs per SM +8 %).
 #ifndef BPD_APPLY_MIN_BLOCKS
 #define BPD_APPLY_MIN_BLOCKS 5
 #endif
 #ifndef BPD_STEP_MIN_BLOCKS
-#define BPD_STEP_MIN_BLOCKS 5
+#define BPD_STEP_MIN_BLOCKS 4
 #endif
 #ifndef BPD_SOFT_STEP_MIN_BLOCKS
 #define BPD_SOFT_STEP_MIN_BLOCKS 5
