@@ -284,6 +284,13 @@ size_t nodes_clear_bytes(int32_t cap) {
          align256(sizeof(int32_t) * 256 * ncap);
 }
 
+// Bytes from nodes.hash that free every node slot (hash and ready words);
+// a slot's transitions are reset by the warp that claims it.
+size_t nodes_free_bytes(int32_t cap) {
+  const size_t ncap = static_cast<size_t>(cap) * kNodesPerEntry;
+  return align256(sizeof(unsigned long long) * ncap) + align256(sizeof(uint32_t) * ncap);
+}
+
 size_t memo_bytes(int32_t cap, int32_t vocab) {
   const size_t ncap = static_cast<size_t>(cap) * kNodesPerEntry;
   return 256 + align256(sizeof(uint32_t) * cap) + align256(sizeof(uint64_t) * cap) +
@@ -467,6 +474,10 @@ __device__ int32_t node_intern(const Nodes& nd, const int32_t* c, uint64_t h, in
     }
     cur = __shfl_sync(kAll, cur, 0);
     if (cur == 0ull) {  // this warp claimed the slot: write the key, then publish it
+      // the slot may have held a node before the table was started over (only
+      // its hash and ready words are cleared then): no transition is known yet
+      int32_t* tr = nd.trans + static_cast<int64_t>(e) * 256;
+      for (int k = lane; k < 256; k += 32) tr[k] = kTransUnknown;
       int32_t* key = nd.key + static_cast<int64_t>(e) * NCFG;
       for (int k = lane; k < NCFG; k += 32) key[k] = canon_word(c, k);
       __threadfence();
@@ -1057,7 +1068,11 @@ __global__ void complete_kernel(bpd_pda_grammar g, const int32_t* __restrict__ p
 // The first launch of every mask call, in place of a memset: zero the call's
 // dedup table, counters and step scratch (Work::clear_bytes from w.dedup)
 // and, when the previous call found the transition cache full (a node it
-// could not intern), the whole node table -- so a grammar whose walks keep
+// could not intern), every node slot's hash and ready words (768 KB at the
+// default capacity; a claimed slot's transitions are reset by the warp that
+// claims it, and no walk reaches a node of the old table: walks start at
+// nodes of the running call and follow transitions stored since the table
+// started over) -- so a grammar whose walks keep
 // reaching new config-sets starts each call with room instead of falling
 // back to direct walks for good. Every CTA reads the flag before it counts
 // itself done, and the last CTA out clears flag and count, so all CTAs act
@@ -1081,14 +1096,19 @@ __global__ void __launch_bounds__(kPrologueThreads)
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t done = atomicAdd(memo.epoch + kHdrPrologueDone, 1u);
+    uint32_t done;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(done)
+                 : "l"(memo.epoch + kHdrPrologueDone)
+                 : "memory");
     if (done == gridDim.x - 1u) {
       memo.epoch[kHdrNodesFull] = 0u;
       memo.epoch[kHdrPrologueDone] = 0u;
     }
   }
 }
+
+constexpr int kPrologueBlocks = 16;
 
 bpd_status check_grammar(const bpd_pda_grammar* g) {
   BPD_REQUIRE(g != nullptr, "null grammar");
@@ -1118,8 +1138,8 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
   Memo memo = memo_view(memo_mem, cap, g->vocab_size);
   Work w = work_view(workspace, batch, g->vocab_size);
   const int32_t sms = sm_count();
-  prologue_kernel<<<sms, kPrologueThreads, 0, st>>>(
-      memo, w, (BPD_PDA_NODES && memo.nodes.cap > 0) ? nodes_clear_bytes(cap) : 0);
+  prologue_kernel<<<kPrologueBlocks, kPrologueThreads, 0, st>>>(
+      memo, w, (BPD_PDA_NODES && memo.nodes.cap > 0) ? nodes_free_bytes(cap) : 0);
   rc = check_launch("pda prologue_kernel");
   if (rc) return rc;
   lookup_kernel<<<(batch + kLookupWarps - 1) / kLookupWarps, kLookupWarps * 32, 0, st>>>(

@@ -582,14 +582,19 @@ struct DenseCommit {
 // fused dense step -11 % in late steps (the pipelined tile loop), mask-only
 // launches -5 % over a config-2 generation (pipelined too; +11 % on the first
 // step alone), fused soft step -7 % over a generation, soft apply -7 %.
-// The fused (non-soft) step then went to 64 registers (4 CTAs per SM, no
-// spills): -1 % on the config-2 step with the .cg stream (85.8 against
-// 86.8 µs over the first 20 steps of a generation; 6 CTAs per SM +8 %).
+// The in-place fused (non-soft) step then went to 64 registers (4 CTAs per
+// SM): -1 % on the config-2 step with the .cg stream (85.8 against 86.8 µs
+// over the first 20 steps of a generation; 6 CTAs per SM +8 %); the step on
+// values read from another buffer (the *_from entry points) stays at 5 CTAs
+// per SM, where 4 cost it 13 % (74.5 against 66.0 µs, tokens-only config 2).
 #ifndef BPD_APPLY_MIN_BLOCKS
 #define BPD_APPLY_MIN_BLOCKS 5
 #endif
 #ifndef BPD_STEP_MIN_BLOCKS
 #define BPD_STEP_MIN_BLOCKS 4
+#endif
+#ifndef BPD_STEP_FROM_MIN_BLOCKS
+#define BPD_STEP_FROM_MIN_BLOCKS 5
 #endif
 #ifndef BPD_SOFT_STEP_MIN_BLOCKS
 #define BPD_SOFT_STEP_MIN_BLOCKS 5
@@ -712,7 +717,9 @@ inline StepScratch step_scratch_view(void* base, int32_t batch) {
 // T), or nowhere when `logits` is nullptr.
 template <typename T, typename S, bool kInPlace, bool kVec, class Rows, class Commit>
 __global__ void __launch_bounds__(kThreads,
-                                  Rows::kSoft ? BPD_SOFT_STEP_MIN_BLOCKS : BPD_STEP_MIN_BLOCKS)
+                                  Rows::kSoft ? BPD_SOFT_STEP_MIN_BLOCKS
+                                  : kInPlace  ? BPD_STEP_MIN_BLOCKS
+                                              : BPD_STEP_FROM_MIN_BLOCKS)
     stream_step_kernel(T* __restrict__ logits, int64_t row_stride, const S* __restrict__ src,
                        int64_t src_stride, const int64_t* __restrict__ src_rows, int32_t V,
                        Rows rows, Commit commit, typename Dt<T>::Bits fill, int32_t chunk,
