@@ -1076,7 +1076,7 @@ __global__ void complete_kernel(bpd_pda_grammar g, const int32_t* __restrict__ p
 // reaching new config-sets starts each call with room instead of falling
 // back to direct walks for good. Every CTA reads the flag before it counts
 // itself done, and the last CTA out clears flag and count, so all CTAs act
-// on the same flag value.
+// on the same flag value (when the flag is unset no CTA counts).
 constexpr int kPrologueThreads = 256;
 
 __global__ void __launch_bounds__(kPrologueThreads)
@@ -1086,14 +1086,13 @@ __global__ void __launch_bounds__(kPrologueThreads)
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   uint4* wz = reinterpret_cast<uint4*>(w.dedup);
   for (size_t i = tid; i < w.clear_bytes / 16; i += stride) wz[i] = zero;
-  if (memo.cap == 0) return;
-  __shared__ uint32_t full;
-  if (threadIdx.x == 0) full = *reinterpret_cast<volatile uint32_t*>(memo.epoch + kHdrNodesFull);
-  __syncthreads();
-  if (full != 0u && node_bytes != 0) {
-    uint4* nz = reinterpret_cast<uint4*>(memo.nodes.hash);
-    for (size_t i = tid; i < node_bytes / 16; i += stride) nz[i] = zero;
-  }
+  if (memo.cap == 0 || node_bytes == 0) return;
+  // nothing writes the flag while the prologue runs, so every thread of the
+  // grid reads the same value: unset (the usual case), nothing more to do
+  const uint32_t full = *reinterpret_cast<volatile uint32_t*>(memo.epoch + kHdrNodesFull);
+  if (full == 0u) return;
+  uint4* nz = reinterpret_cast<uint4*>(memo.nodes.hash);
+  for (size_t i = tid; i < node_bytes / 16; i += stride) nz[i] = zero;
   __syncthreads();
   if (threadIdx.x == 0) {
     uint32_t done;

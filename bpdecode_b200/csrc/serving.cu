@@ -61,47 +61,73 @@ struct TurnArgs {
   uint8_t* retired;
 };
 
-// One CTA of 1024 threads. Phase 1 (a thread per row): draw, retire, write
-// the new kind and dense state. Phase 2 (a warp per admitted PDA row): its
-// fresh config-set. Phase 3: the row lists, an order-preserving compaction
-// (ballot + warp prefix sums + a running base per 1024 rows).
+// One CTA of 1024 threads; thread t handles rows t, t + 1024, ... in every
+// phase. Phase 1: draw, retire, write the new kind and dense state; the
+// thread keeps its rows' kinds (up to kRowsInRegs rows a thread) for phase 3,
+// and admitted PDA rows go to a shared list. Phase 2 (a warp per listed row):
+// the fresh config-sets. Phase 3: the row lists, an order-preserving
+// compaction (ballot + warp prefix sums + a running base per 1024 rows).
+constexpr int kRowsInRegs = 8;       // rows up to 8192 keep their kinds in registers
+constexpr int kAdmitList = 2048;     // admitted PDA rows listed in shared memory
+
 __global__ void __launch_bounds__(kTurnThreads) turnover_kernel(TurnArgs a) {
   __shared__ int32_t warp_d[kTurnThreads / 32], warp_p[kTurnThreads / 32];
-  __shared__ int32_t base_d, base_p;
+  __shared__ int32_t base_d, base_p, n_admit;
+  __shared__ int32_t admit[kAdmitList];
   const int32_t tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint64_t step = *a.step;
-  for (int32_t r = tid; r < a.rows; r += kTurnThreads) {
-    const bool out = unit_draw(a.seed, step, r, 0) < a.evict_prob;
-    a.retired[r] = out ? 1 : 0;
-    if (!out) continue;
-    const float u = unit_draw(a.seed, step, r, 1);
-    int32_t k = 1, g = -1;
-    if (u < a.p_regex) {
-      k = 0;
-      g = min(a.n_regex - 1, static_cast<int32_t>(unit_draw(a.seed, step, r, 2) *
-                                                  static_cast<float>(a.n_regex)));
-    } else if (a.schema_grammar >= 0 && u < a.p_regex + a.p_schema) {
-      k = 0;
-      g = a.schema_grammar;
-    }
-    a.kind[r] = k;
-    a.state_pool[r] = k == 0 ? a.dense_starts[g] : -2;  // FREE for a PDA request
-    if (k == 1) a.broken[r] = 0;
-  }
-  __syncthreads();
-  for (int32_t r = warp; r < a.rows; r += kTurnThreads / 32) {
-    if (a.retired[r] == 0 || a.kind[r] != 1) continue;
-    int32_t* c = a.config_pool + static_cast<int64_t>(r) * NCFG;
-    for (int k = lane; k < NCFG; k += 32) c[k] = a.pda_init[k];
-  }
   if (tid == 0) {
     base_d = 0;
     base_p = 0;
+    n_admit = 0;
   }
   __syncthreads();
-  for (int32_t r0 = 0; r0 < a.rows; r0 += kTurnThreads) {
+  const uint64_t step = *a.step;
+  int32_t kinds[kRowsInRegs];
+#pragma unroll
+  for (int j = 0; j < kRowsInRegs; ++j) kinds[j] = -1;
+  for (int32_t r = tid, j = 0; r < a.rows; r += kTurnThreads, ++j) {
+    const bool out = unit_draw(a.seed, step, r, 0) < a.evict_prob;
+    int32_t k = out ? 1 : a.kind[r];
+    a.retired[r] = out ? 1 : 0;
+    if (out) {
+      const float u = unit_draw(a.seed, step, r, 1);
+      int32_t g = -1;
+      if (u < a.p_regex) {
+        k = 0;
+        g = min(a.n_regex - 1, static_cast<int32_t>(unit_draw(a.seed, step, r, 2) *
+                                                    static_cast<float>(a.n_regex)));
+      } else if (a.schema_grammar >= 0 && u < a.p_regex + a.p_schema) {
+        k = 0;
+        g = a.schema_grammar;
+      }
+      a.kind[r] = k;
+      a.state_pool[r] = k == 0 ? a.dense_starts[g] : -2;  // FREE for a PDA request
+      if (k == 1) {
+        a.broken[r] = 0;
+        const int32_t at = atomicAdd(&n_admit, 1);
+        if (at < kAdmitList) admit[at] = r;
+      }
+    }
+    if (j < kRowsInRegs) kinds[j] = k;
+  }
+  __syncthreads();
+  if (n_admit <= kAdmitList) {
+    for (int32_t i = warp; i < n_admit; i += kTurnThreads / 32) {
+      int32_t* c = a.config_pool + static_cast<int64_t>(admit[i]) * NCFG;
+      for (int k = lane; k < NCFG; k += 32) c[k] = a.pda_init[k];
+    }
+  } else {
+    for (int32_t r = warp; r < a.rows; r += kTurnThreads / 32) {
+      if (a.retired[r] == 0 || a.kind[r] != 1) continue;
+      int32_t* c = a.config_pool + static_cast<int64_t>(r) * NCFG;
+      for (int k = lane; k < NCFG; k += 32) c[k] = a.pda_init[k];
+    }
+  }
+  int32_t j = 0;
+  for (int32_t r0 = 0; r0 < a.rows; r0 += kTurnThreads, ++j) {
     const int32_t r = r0 + tid;
-    const int32_t k = r < a.rows ? a.kind[r] : -1;
+    int32_t k = -1;
+    if (r < a.rows) k = j < kRowsInRegs ? kinds[j < kRowsInRegs ? j : 0] : a.kind[r];
     const uint32_t bd = __ballot_sync(0xFFFFFFFFu, k == 0), bp = __ballot_sync(0xFFFFFFFFu, k == 1);
     if (lane == 0) {
       warp_d[warp] = __popc(bd);
