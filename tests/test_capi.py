@@ -45,3 +45,41 @@ def test_header_compiles_as_c() -> None:
     r = subprocess.run(["gcc", "-std=c99", "-fsyntax-only", "-x", "c", src], capture_output=True,
                        text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_serving_and_row_count_entry_points_check_arguments() -> None:
+    """The device-turnover and device-row-count entry points reject bad
+    arguments before anything is enqueued (no device needed)."""
+    from bpdecode_b200 import _capi
+
+    L = _capi.lib()
+    fake = 256  # a non-null pointer value: never dereferenced on these paths
+    args = [8, 1, fake, 0.1, 0.5, 0.3, 8, 8] + [fake] * 10 + [None]
+    bad_prob = list(args)
+    bad_prob[3] = 1.5
+    assert L.bpd_serving_turnover(*bad_prob) == 1
+    assert b"probabilities" in L.bpd_last_error()
+    bad_mix = list(args)
+    bad_mix[4], bad_mix[5] = 0.8, 0.4
+    assert L.bpd_serving_turnover(*bad_mix) == 1
+    no_regex = list(args)
+    no_regex[6] = 0
+    assert L.bpd_serving_turnover(*no_regex) == 1
+    assert b"n_regex" in L.bpd_last_error()
+    null_ptr = list(args)
+    null_ptr[10] = None
+    assert L.bpd_serving_turnover(*null_ptr) == 1
+    assert b"null pointer" in L.bpd_last_error()
+    assert L.bpd_serving_turnover(0, 1, None, 0.1, 0.5, 0.3, 8, 8, *([None] * 11)) == 0
+    assert L.bpd_serving_gather_tokens(4, None, fake, fake, fake, fake, fake, None) == 1
+    assert L.bpd_serving_gather_tokens(0, None, None, None, None, None, None, None) == 0
+    # the *_from_n steps need their device row count
+    assert L.bpd_soft_step_greedy_from_n(fake, 0, 16, None, None, 0, 4, None, 16, fake, None,
+                                         fake, fake, 4, fake, 2, 1.0, fake, None, 0, fake,
+                                         None) == 1
+    assert b"row count" in L.bpd_last_error()
+    g = _capi.PdaGrammar()
+    assert L.bpd_pda_step_greedy_from_n(C.byref(g), fake, 0, 16, None, None, 0, fake, None,
+                                        None, 4, None, None, 0, fake, 0.0, fake, None, 0,
+                                        None) == 1
+    assert b"row count" in L.bpd_last_error()

@@ -86,7 +86,9 @@ def _host_pda(vocab):
                    vocab.eos_id)
 
 
-def test_device_loop_matches_oracle() -> None:
+@pytest.mark.parametrize("dtype,steps", [(torch.bfloat16, 48), (torch.float32, 16),
+                                         (torch.float16, 16)])
+def test_device_loop_matches_oracle(dtype: torch.dtype, steps: int) -> None:
     """The device-turnover loop: before every step the row lists and counts
     match the kinds; every row's token and next state equal the C oracle's
     from that row's state (soft bias on fp32 working values for dense rows,
@@ -100,7 +102,7 @@ def test_device_loop_matches_oracle() -> None:
 
     orc = Oracle()
     dense, pda, vocab = _grammars(4096)
-    rows, steps = 160, 48
+    rows = 160
     loop = DeviceServingLoop(rows, dense, pda, n_regex=len(DENSE_PATTERNS), seed=21)
     tn = loop.dense._t.tok_next.cpu().numpy()
     la = loop.dense._t.lookahead.cpu().numpy()
@@ -110,8 +112,7 @@ def test_device_loop_matches_oracle() -> None:
     gen = torch.Generator(device="cuda").manual_seed(77)
     turned = 0
     for step in range(steps):
-        logits = (torch.randn(rows, vocab.size, generator=gen, device="cuda") * 2).to(
-            torch.bfloat16)
+        logits = (torch.randn(rows, vocab.size, generator=gen, device="cuda") * 2).to(dtype)
         kind = loop.kind.cpu().numpy()
         pool, cfgs, broken = (x.cpu().numpy().copy() for x in loop.states())
         d, p = np.flatnonzero(kind == 0), np.flatnonzero(kind == 1)
@@ -153,7 +154,7 @@ def test_device_loop_matches_oracle() -> None:
                 assert pool3[r] == -2 and not broken3[r], (step, r)
                 assert np.array_equal(cfgs3[r], init), (step, r)
     # about 10 % of the rows turn over per step
-    assert 0.06 * rows * steps < turned < 0.14 * rows * steps, turned
+    assert 0.05 * rows * steps < turned < 0.15 * rows * steps, turned
 
 
 def test_device_loop_graph_replay_equals_eager() -> None:
