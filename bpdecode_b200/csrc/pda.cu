@@ -18,10 +18,12 @@
 //   (already set), so one pass that keeps going until it reaches the end of
 //   the list performs the same pushes in the same order.
 // * Mask of a row = for every token, does its byte walk keep the set
-//   non-empty. The walk's first step has only 256 outcomes, so each row first
-//   computes which first bytes survive (256 warp walks) and every token whose
-//   first byte dies is rejected without a walk; single-byte survivors are
-//   accepted; only the rest are walked, a warp per token.
+//   non-empty. The walks go through a transition cache built on the device
+//   (config-sets interned as nodes with 256 byte transitions, each computed
+//   once by the bounded closure), so a token costs a few table reads once
+//   its stretch of the grammar has been visited; without a memo, the first
+//   bytes that keep each set alive are found first (256 warp walks) and only
+//   longer tokens whose first byte survives are walked.
 // * Mask memo in HBM, keyed by the config-set's live content (`saturated` and
 //   words outside the live region do not affect the mask and are not part of
 //   the key): an open-addressing table of {hash, canonical 266-int key, packed
@@ -31,10 +33,12 @@
 //   like the dense path.
 //
 // Per mask call (all on the caller's stream, no host sync):
-//   memset(dedup) -> lookup_kernel (memo probe, dedup, memo claim)
-//   -> first_byte_kernel -> compute_kernel (misses only; both exit at once when
-//   every row hit) -> apply, or the fused step (apply + argmax, and the warp
-//   that finishes a row advances its config-set by the winning token).
+//   prologue_kernel (clears the call's workspace; the transition cache when
+//   it filled up) -> lookup_kernel (memo probe, dedup, memo claim)
+//   -> [first_byte_kernel, without a memo] -> compute_kernel (misses only; it
+//   ends at once when every row hit) -> apply, or the fused step (apply +
+//   argmax, and the warp that finishes a row advances its config-set by the
+//   winning token).
 #include <cuda.h>
 
 #include <algorithm>
@@ -896,10 +900,11 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
 
 constexpr int kLookupWarps = 4;
 
-// The mask pipeline's kernels, in stream order after a memset of the call's
-// dedup table and counters: memo lookup and in-batch dedup (a warp per row),
-// first bytes of the representatives, their allow bits. With every row a
-// memo hit the last two find no items and end at once.
+// The mask pipeline's kernels, in stream order after prologue_kernel clears
+// the call's dedup table and counters: memo lookup and in-batch dedup (a warp
+// per row), first bytes of the representatives (without a memo only), their
+// allow bits. With every row a memo hit the last two find no items and end
+// at once.
 __global__ void __launch_bounds__(kLookupWarps * 32)
     lookup_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
                   const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
@@ -1121,7 +1126,7 @@ bpd_status check_grammar(const bpd_pda_grammar* g) {
   return BPD_OK;
 }
 
-// memset(dedup) + lookup + claim + compute: leaves every row's allow bits
+// prologue + lookup + claim + compute: leaves every row's allow bits
 // resolvable through (memo, work).
 bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, const int64_t* slots,
                              const uint8_t* broken, int32_t batch, void* memo_mem, int32_t cap,
