@@ -259,6 +259,9 @@ class DeviceServingLoop:
         (``[rows, V]``, any float dtype; not modified)."""
         R = self.rows
         t = self.dense._t
+        if logits.dim() != 2 or int(logits.shape[0]) < R:
+            raise RuntimeError(f"bpdecode_b200: logits must be [>= {R}, vocab], got "
+                               f"{tuple(logits.shape)}")
         code, _, _ = _source_args(logits, t.vocab_size, R, self.dense_rows, None, self.device)
         st = _stream(logits)
         L = _capi.lib()
