@@ -147,6 +147,9 @@ class MixedServingLoop:
         """Greedy tokens (int64 ``[rows]``) for one step of ``logits``
         (``[rows, V]``, any float dtype; not modified)."""
         d_rows, d_idx, d_sl, p_rows, p_idx, p_sl = self._step_args
+        if logits.dim() != 2 or int(logits.shape[0]) < self.rows:
+            raise RuntimeError(f"bpdecode_b200: logits must be [>= {self.rows}, vocab], got "
+                               f"{tuple(logits.shape)}")
         tokens = torch.empty(self.rows, dtype=torch.int64, device=self.device)
         if len(d_rows):
             if self.fused:
