@@ -105,6 +105,41 @@ bpd_status with_dtype(int32_t dtype, const char* what, F&& f, const char* kind =
 
 constexpr size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
 
+// Programmatic dependent launch: the per-step kernels are launched with the
+// programmatic-serialization attribute, start their grid's successor early
+// (pdl_trigger) and wait for their predecessor to complete, with its memory
+// visible, before their first global memory access (pdl_wait); only shared
+// memory set-up comes before the wait. A dependent grid is scheduled only once
+// every CTA of its predecessor has started, so CTAs blocked in the wait never
+// keep a predecessor's CTAs off the SMs. Launched without the attribute (or
+// after a kernel that never triggers) the wait returns at once.
+#ifndef BPD_PDL
+#define BPD_PDL 1
+#endif
+
+__device__ __forceinline__ void pdl_wait() {
+  if constexpr (BPD_PDL) asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  if constexpr (BPD_PDL) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... K, typename... A>
+cudaError_t launch_pdl(void (*kernel)(K...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = BPD_PDL ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+
 __device__ __forceinline__ uint32_t vec_word(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }

@@ -910,6 +910,8 @@ __global__ void __launch_bounds__(kLookupWarps * 32)
                   const int64_t* __restrict__ slots, const uint8_t* __restrict__ broken,
                   int32_t batch, Memo memo, Work w, const int32_t* __restrict__ nrows) {
   __shared__ int32_t buf[kLookupWarps][2][NCFG];
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5;
   const int32_t b = blockIdx.x * kLookupWarps + warp;
   const int32_t n = nrows != nullptr ? min(batch, *nrows) : batch;
@@ -920,6 +922,8 @@ __global__ void __launch_bounds__(kThreads)
     first_byte_kernel(bpd_pda_grammar g, const int32_t* __restrict__ pool,
                       const int64_t* __restrict__ slots, Work w) {
   __shared__ int32_t scratch[kWarps][NCFG];
+  pdl_trigger();
+  pdl_wait();
   first_byte_items(g, pool, slots, w, scratch[threadIdx.x >> 5]);
 }
 
@@ -930,6 +934,8 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ uint32_t first[8];
   __shared__ int32_t strans[256];
   __shared__ int32_t s_item;
+  pdl_trigger();
+  pdl_wait();
   compute_items(g, pool, slots, memo, w, first_valid != 0, buf, first, strans, s_item);
   // the last kernel of every mask call: the next call gets a new tag (the
   // lookups of this call, which read the old epoch, have all finished)
@@ -1086,6 +1092,8 @@ constexpr int kPrologueThreads = 256;
 
 __global__ void __launch_bounds__(kPrologueThreads)
     prologue_kernel(Memo memo, Work w, size_t node_bytes) {
+  pdl_trigger();
+  pdl_wait();  // the previous call's kernels may still use this workspace
   const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
@@ -1142,12 +1150,15 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
   Memo memo = memo_view(memo_mem, cap, g->vocab_size);
   Work w = work_view(workspace, batch, g->vocab_size);
   const int32_t sms = sm_count();
-  prologue_kernel<<<kPrologueBlocks, kPrologueThreads, 0, st>>>(
-      memo, w, (BPD_PDA_NODES && memo.nodes.cap > 0) ? nodes_free_bytes(cap) : 0);
+  const size_t node_bytes = (BPD_PDA_NODES && memo.nodes.cap > 0) ? nodes_free_bytes(cap) : 0;
+  cudaError_t e = launch_pdl(prologue_kernel, dim3(kPrologueBlocks), dim3(kPrologueThreads), 0, st,
+                             memo, w, node_bytes);
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "pda prologue_kernel: %s", cudaGetErrorString(e));
   rc = check_launch("pda prologue_kernel");
   if (rc) return rc;
-  lookup_kernel<<<(batch + kLookupWarps - 1) / kLookupWarps, kLookupWarps * 32, 0, st>>>(
-      *g, pool, slots, broken, batch, memo, w, nrows);
+  e = launch_pdl(lookup_kernel, dim3((batch + kLookupWarps - 1) / kLookupWarps),
+                 dim3(kLookupWarps * 32), 0, st, *g, pool, slots, broken, batch, memo, w, nrows);
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "pda lookup_kernel: %s", cudaGetErrorString(e));
   rc = check_launch("pda lookup_kernel");
   if (rc) return rc;
   // With a transition cache the compute walks take every token from its
@@ -1156,11 +1167,15 @@ bpd_status run_mask_pipeline(const bpd_pda_grammar* g, const int32_t* pool, cons
   // any other byte are rejected without a walk.
   const bool nodes = BPD_PDA_NODES && memo.nodes.cap > 0;
   if (!nodes) {
-    first_byte_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, w);
+    e = launch_pdl(first_byte_kernel, dim3(sms * 2), dim3(kThreads), 0, st, *g, pool, slots, w);
+    if (e != cudaSuccess)
+      return fail(BPD_ERR_CUDA, "pda first_byte_kernel: %s", cudaGetErrorString(e));
     rc = check_launch("pda first_byte_kernel");
     if (rc) return rc;
   }
-  compute_kernel<<<sms * 2, kThreads, 0, st>>>(*g, pool, slots, memo, w, nodes ? 0 : 1);
+  e = launch_pdl(compute_kernel, dim3(sms * 2), dim3(kThreads), 0, st, *g, pool, slots, memo, w,
+                 nodes ? 0 : 1);
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "pda compute_kernel: %s", cudaGetErrorString(e));
   rc = check_launch("pda compute_kernel");
   if (rc) return rc;
   *memo_out = memo;

@@ -667,6 +667,8 @@ __global__ void __launch_bounds__(kThreads, BPD_APPLY_MIN_BLOCKS)
     fill_init<T>(smem, fill);
     __syncthreads();
   }
+  pdl_trigger();
+  pdl_wait();  // the rows' states / allow rows come from the kernels before
   const int32_t row = blockIdx.x / chunks_per_row;
   const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
   const WarpShare ws = warp_share<T, kVec>(c0, min(V, c0 + chunk));
@@ -728,14 +730,17 @@ __global__ void __launch_bounds__(kThreads,
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ unsigned long long warp_q[kWarps];
   __shared__ uint32_t warps_done;
-  // rows at or past a device-held row count are not part of this call (the
-  // *_from_n entry points; the in-place steps never take one)
-  if constexpr (!kInPlace) {
-    if (nrows != nullptr && static_cast<int32_t>(blockIdx.x / chunks_per_row) >= *nrows) return;
-  }
   if (threadIdx.x == 0) warps_done = 0u;
   if constexpr (kVec) fill_init<T>(smem, fill);
   __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // states, allow rows and the row count come from the kernels before
+  // rows at or past a device-held row count are not part of this call (the
+  // *_from_n entry points; the in-place steps never take one); the whole CTA
+  // leaves together, and no barrier follows
+  if constexpr (!kInPlace) {
+    if (nrows != nullptr && static_cast<int32_t>(blockIdx.x / chunks_per_row) >= *nrows) return;
+  }
   const int32_t row = blockIdx.x / chunks_per_row;
   const int32_t c0 = (blockIdx.x - row * chunks_per_row) * chunk;
   const WarpShare sh = warp_share<T, kVec>(c0, min(V, c0 + chunk));
@@ -815,11 +820,15 @@ bpd_status launch_stream_apply(void* logits, int64_t row_stride, int32_t batch, 
   const auto fill = Dt<T>::from_float_host(neg_inf);
   T* lg = static_cast<T*>(logits);
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    stream_apply_kernel<T, true, Rows><<<static_cast<unsigned>(grid), kThreads, kFillBytes, st>>>(
-        lg, row_stride, V, rows, fill, chunk, chunks);
+    const cudaError_t e = launch_pdl(stream_apply_kernel<T, true, Rows>,
+                                     dim3(static_cast<unsigned>(grid)), dim3(kThreads), kFillBytes,
+                                     st, lg, row_stride, V, rows, fill, chunk, chunks);
+    if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   } else {
-    stream_apply_kernel<T, false, Rows><<<static_cast<unsigned>(grid), kThreads, 0, st>>>(
-        lg, row_stride, V, rows, fill, chunk, chunks);
+    const cudaError_t e = launch_pdl(stream_apply_kernel<T, false, Rows>,
+                                     dim3(static_cast<unsigned>(grid)), dim3(kThreads), 0, st, lg,
+                                     row_stride, V, rows, fill, chunk, chunks);
+    if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   }
   return check_launch(what);
 }
@@ -840,17 +849,21 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   const StepScratch ws = step_scratch_view(scratch, batch);
   T* lg = static_cast<T*>(logits);
   const size_t smem = kFillBytes + Commit::kSmemBytes;
+  const int64_t* no_rows = nullptr;
+  const int32_t* no_count = nullptr;
+  cudaError_t e;
   if (vec_ok<Rows>(logits, row_stride, sizeof(T), V)) {
-    stream_step_kernel<T, T, true, true, Rows, Commit>
-        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(lg, row_stride, lg, row_stride,
-                                                               nullptr, V, rows, commit, fill,
-                                                               chunk, cpr, ws, nullptr);
+    e = launch_pdl(stream_step_kernel<T, T, true, true, Rows, Commit>,
+                   dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, st, lg, row_stride,
+                   static_cast<const T*>(lg), row_stride, no_rows, V, rows, commit, fill, chunk,
+                   cpr, ws, no_count);
   } else {
-    stream_step_kernel<T, T, true, false, Rows, Commit>
-        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(lg, row_stride, lg, row_stride,
-                                                               nullptr, V, rows, commit, fill,
-                                                               chunk, cpr, ws, nullptr);
+    e = launch_pdl(stream_step_kernel<T, T, true, false, Rows, Commit>,
+                   dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, st, lg, row_stride,
+                   static_cast<const T*>(lg), row_stride, no_rows, V, rows, commit, fill, chunk,
+                   cpr, ws, no_count);
   }
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return check_launch(what);
 }
 
@@ -877,17 +890,17 @@ bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int
                    (out == nullptr || rows_aligned(out, out_stride, sizeof(float))) &&
                    (!Rows::kSoft || V % 4 == 0);
   const S* sp = static_cast<const S*>(src);
+  cudaError_t e;
   if (vec) {
-    stream_step_kernel<float, S, false, true, Rows, Commit>
-        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(out, out_stride, sp, src_stride,
-                                                               src_rows, V, rows, commit, fill,
-                                                               chunk, cpr, ws, nrows);
+    e = launch_pdl(stream_step_kernel<float, S, false, true, Rows, Commit>,
+                   dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, st, out, out_stride,
+                   sp, src_stride, src_rows, V, rows, commit, fill, chunk, cpr, ws, nrows);
   } else {
-    stream_step_kernel<float, S, false, false, Rows, Commit>
-        <<<static_cast<unsigned>(grid), kThreads, smem, st>>>(out, out_stride, sp, src_stride,
-                                                               src_rows, V, rows, commit, fill,
-                                                               chunk, cpr, ws, nrows);
+    e = launch_pdl(stream_step_kernel<float, S, false, false, Rows, Commit>,
+                   dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, st, out, out_stride,
+                   sp, src_stride, src_rows, V, rows, commit, fill, chunk, cpr, ws, nrows);
   }
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return check_launch(what);
 }
 
