@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(kTurnThreads) turnover_kernel(TurnArgs a) {
     n_admit = 0;
   }
   __syncthreads();
+  pdl_trigger();
+  pdl_wait();  // kinds, pools and lists are the step kernels' until they end
   const uint64_t step = *a.step;
   int32_t kinds[kRowsInRegs];
 #pragma unroll
@@ -164,6 +166,8 @@ __global__ void gather_tokens_kernel(int32_t rows, const int64_t* __restrict__ d
                                      const int64_t* __restrict__ dense_tok,
                                      const int64_t* __restrict__ pda_tok,
                                      int64_t* __restrict__ tokens_out) {
+  pdl_trigger();
+  pdl_wait();
   const int32_t b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= rows) return;
   const int32_t nd = min(counts[0], rows), np = min(counts[1], rows);
@@ -201,7 +205,9 @@ extern "C" bpd_status bpd_serving_turnover(
              n_regex,    schema_grammar,       dense_starts, pda_init, kind,
              state_pool, config_pool,          broken,       dense_rows, pda_rows,
              counts,     retired};
-  turnover_kernel<<<1, kTurnThreads, 0, as_stream(stream)>>>(a);
+  const cudaError_t e = launch_pdl(turnover_kernel, dim3(1), dim3(kTurnThreads), 0,
+                                   as_stream(stream), a);
+  if (e != cudaSuccess) return fail(BPD_ERR_CUDA, "turnover_kernel: %s", cudaGetErrorString(e));
   return check_launch("turnover_kernel");
 }
 
@@ -213,7 +219,10 @@ extern "C" bpd_status bpd_serving_gather_tokens(int32_t rows, const int64_t* den
   if (rows == 0) return BPD_OK;
   BPD_REQUIRE(dense_rows && pda_rows && counts && dense_tok && pda_tok && tokens_out,
               "bpd_serving_gather_tokens: null pointer");
-  gather_tokens_kernel<<<(rows + 255) / 256, 256, 0, as_stream(stream)>>>(
-      rows, dense_rows, pda_rows, counts, dense_tok, pda_tok, tokens_out);
+  const cudaError_t e = launch_pdl(gather_tokens_kernel, dim3((rows + 255) / 256), dim3(256), 0,
+                                   as_stream(stream), rows, dense_rows, pda_rows, counts,
+                                   dense_tok, pda_tok, tokens_out);
+  if (e != cudaSuccess)
+    return fail(BPD_ERR_CUDA, "gather_tokens_kernel: %s", cudaGetErrorString(e));
   return check_launch("gather_tokens_kernel");
 }
