@@ -137,7 +137,9 @@ cudaError_t launch_pdl(void (*kernel)(K...), dim3 grid, dim3 block, size_t smem,
   attr[0].val.programmaticStreamSerializationAllowed = BPD_PDL ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+  if (e != cudaSuccess) (void)cudaGetLastError();  // reported here, not by a later check
+  return e;
 }
 
 __device__ __forceinline__ uint32_t vec_word(const uint4& v, int i) {
