@@ -520,7 +520,7 @@ __device__ int32_t node_intern(const Nodes& nd, const int32_t* c, uint64_t h, in
 // transition is read from the table; an unknown one is computed here (the
 // bounded closure, w_advance_byte, on q's content) and stored.
 __device__ int32_t node_step(const bpd_pda_grammar& g, const Nodes& nd, int32_t q, int byte,
-                             int32_t* cur, int32_t* next, int lane) {
+                             int32_t* cur, int32_t* next, int lane, bool key_ready = false) {
   if (q < 0 || q >= nd.cap) return -2;  // not a node: callers never pass one
   int32_t* slot = nd.trans + static_cast<int64_t>(q) * 256 + byte;
   int32_t v = 0;
@@ -542,11 +542,13 @@ __device__ int32_t node_step(const bpd_pda_grammar& g, const Nodes& nd, int32_t 
   if (!own && v >= kTransNode && v - kTransNode < nd.cap) return v - kTransNode;
   // compute it (owner, or after a wait that ran out: then without storing);
   // q came from a transition another warp may have stored just now: order
-  // the key's reads after it
-  __threadfence();
-  const int32_t* key = nd.key + static_cast<int64_t>(q) * NCFG;
-  for (int k = lane; k < NCFG; k += 32) cur[k] = __ldcg(key + k);
-  __syncwarp();
+  // the key's reads after it (unless the caller already holds q's key in cur)
+  if (!key_ready) {
+    __threadfence();
+    const int32_t* key = nd.key + static_cast<int64_t>(q) * NCFG;
+    for (int k = lane; k < NCFG; k += 32) cur[k] = __ldcg(key + k);
+    __syncwarp();
+  }
   int32_t r = -1;
   if (w_advance_byte<false>(g, cur, next, byte, lane)) {
     const int32_t e = node_intern(nd, next, w_hash(next, lane), lane);
@@ -809,9 +811,15 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
       // first-byte transitions of a representative's node, 4 bytes a warp
       const int32_t nd = w.node[w.reps[item / kPrefillItems]];
       if (nd >= 0) {
+        // the node's key once for the warp's 4 bytes (the node was interned by
+        // the lookup kernel, which has completed; node_step leaves cur intact)
+        int32_t* cur = buf[warp][0];
+        const int32_t* key = memo.nodes.key + static_cast<int64_t>(nd) * NCFG;
+        for (int k = lane; k < NCFG; k += 32) cur[k] = __ldcg(key + k);
+        __syncwarp();
         const int32_t b0 = (item % kPrefillItems) * (kWarps * 4) + warp * 4;
-        for (int k = 0; k < 4; ++k) node_step(g, memo.nodes, nd, b0 + k, buf[warp][0],
-                                              buf[warp][1], lane);
+        for (int k = 0; k < 4; ++k)
+          node_step(g, memo.nodes, nd, b0 + k, cur, buf[warp][1], lane, true);
       }
       continue;
     }
@@ -831,17 +839,28 @@ __device__ __forceinline__ void compute_items(const bpd_pda_grammar& g,
     const bool eos_ok = w.eos_ok[b] != 0;
     const bool nonempty = n_of(base) > 0;
     uint32_t* out = rep_bits(memo, w, b);
+    // each lane's token offsets are loaded one iteration ahead
+    int32_t n_o0 = 0, n_o1 = 0;
+    if (c0 + warp * 32 + lane < c1) {
+      n_o0 = __ldg(g.tok_offsets + c0 + warp * 32 + lane);
+      n_o1 = __ldg(g.tok_offsets + c0 + warp * 32 + lane + 1);
+    }
     for (int32_t t0 = c0 + warp * 32; t0 < c1; t0 += kWarps * 32) {
       const int32_t t = t0 + lane;
       bool ok = false, walk = false;
-      int32_t o0 = 0, o1 = 0;
+      int32_t o0 = n_o0, o1 = n_o1;
+      if (t + kWarps * 32 < c1) {
+        n_o0 = __ldg(g.tok_offsets + t + kWarps * 32);
+        n_o1 = __ldg(g.tok_offsets + t + kWarps * 32 + 1);
+      }
       int32_t q = nd0;  // the node a lane's walk starts from (with a node)
-      if (t < c1) {
+      if (t >= c1) {
+        o0 = o1 = 0;
+      } else {
         if (t == g.eos_id) {
           ok = eos_ok;
+          o0 = o1 = 0;
         } else {
-          o0 = __ldg(g.tok_offsets + t);
-          o1 = __ldg(g.tok_offsets + t + 1);
           if (o0 == o1) {
             ok = nonempty;
           } else if (nd0 >= 0) {
