@@ -974,8 +974,19 @@ __device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work
 }
 
 // Row -> its allow words through the memo / workspace (nullptr for broken rows).
+// In place, PDA rows are mostly rejected tiles that go out as bulk fills: a
+// CTA takes twice the dense chunk (8 warp tiles a warp), so fewer CTAs per
+// row meet in the argmax merge (config 4, 256 rows: 39.0 against 40.1-40.8 us
+// per step from a graph, same box; the miss-path workloads unchanged). The
+// step from the model's rows keeps the dense chunk (config-5 serving step
+// 147.8 against 148.4-148.6 us with the larger one).
+#ifndef BPD_PDA_TILES_PER_WARP
+#define BPD_PDA_TILES_PER_WARP 8
+#endif
+
 struct PdaRows {
   static constexpr bool kSoft = false;
+  static constexpr int kTilesPerWarp = BPD_PDA_TILES_PER_WARP;
   Memo memo;
   Work w;
   __device__ __forceinline__ RowInfo operator()(int32_t row) const {

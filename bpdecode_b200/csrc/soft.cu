@@ -109,6 +109,7 @@ __global__ void lookahead_out_kernel(const int32_t* __restrict__ tn, int32_t S, 
 // live) and its lookahead row (the biases); no state = everything -inf.
 struct SoftRows {
   static constexpr bool kSoft = true;
+  static constexpr int kTilesPerWarp = BPD_TILES_PER_WARP;
   const int32_t* pool;
   const int64_t* slots;
   const uint32_t* bits;

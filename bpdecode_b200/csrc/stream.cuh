@@ -538,8 +538,15 @@ __device__ __forceinline__ const uint32_t* state_row(const int32_t* __restrict__
   return (s >= 0 && s < S) ? bits + static_cast<int64_t>(s) * wstride : nullptr;
 }
 
+// Warp tiles each warp streams per CTA when the caller leaves the chunk to
+// stream_chunk (a Rows type may ask for another count).
+#ifndef BPD_TILES_PER_WARP
+#define BPD_TILES_PER_WARP 4
+#endif
+
 struct DenseRows {
   static constexpr bool kSoft = false;
+  static constexpr int kTilesPerWarp = BPD_TILES_PER_WARP;
   const int32_t* pool;
   const int64_t* slots;
   const uint32_t* bits;
@@ -599,9 +606,6 @@ struct DenseCommit {
 #ifndef BPD_SOFT_STEP_MIN_BLOCKS
 #define BPD_SOFT_STEP_MIN_BLOCKS 5
 #endif
-#ifndef BPD_TILES_PER_WARP
-#define BPD_TILES_PER_WARP 4
-#endif
 
 // Chunk of one CTA: `chunks_per_row` CTAs per row when the caller asks for
 // it, else BPD_TILES_PER_WARP warp tiles per warp. Always a multiple of
@@ -612,10 +616,11 @@ struct DenseCommit {
 // rows is not a few CTAs working through their tiles one after another
 // (B = 1, V = 128,256: 13.9 -> 11.9 us per step replayed from a graph).
 template <typename T>
-inline int32_t stream_chunk(int32_t V, int32_t chunks_per_row, int32_t batch = 0) {
+inline int32_t stream_chunk(int32_t V, int32_t chunks_per_row, int32_t batch = 0,
+                            int32_t tiles_per_warp = BPD_TILES_PER_WARP) {
   constexpr int32_t UNIT = tile_elems<T>() * kWarps;
   if (chunks_per_row <= 0) {
-    int32_t tpw = BPD_TILES_PER_WARP;
+    int32_t tpw = tiles_per_warp;
     const int64_t want = static_cast<int64_t>(sm_count());
     while (tpw > 1 && batch > 0 &&
            static_cast<int64_t>(batch) * ((V + UNIT * tpw - 1) / (UNIT * tpw)) < want)
@@ -813,7 +818,7 @@ template <typename T, class Rows>
 bpd_status launch_stream_apply(void* logits, int64_t row_stride, int32_t batch, int32_t V,
                                const Rows& rows, float neg_inf, cudaStream_t st,
                                const char* what) {
-  const int32_t chunk = stream_chunk<T>(V, 0, batch);
+  const int32_t chunk = stream_chunk<T>(V, 0, batch, Rows::kTilesPerWarp);
   const int32_t chunks = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * chunks;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
@@ -841,7 +846,7 @@ bpd_status launch_stream_step(void* logits, int64_t row_stride, int32_t batch, i
   if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
   if (!aligned16(scratch))
     return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
-  const int32_t chunk = stream_chunk<T>(V, chunks_per_row, batch);
+  const int32_t chunk = stream_chunk<T>(V, chunks_per_row, batch, Rows::kTilesPerWarp);
   const int32_t cpr = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * cpr;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
@@ -879,6 +884,7 @@ bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int
   if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
   if (!aligned16(scratch))
     return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
+  // every Rows type takes the dense chunk here (measured best for PDA rows too)
   const int32_t chunk = stream_chunk<float>(V, chunks_per_row, batch);
   const int32_t cpr = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * cpr;
