@@ -86,7 +86,7 @@ def _host_pda(vocab):
                    vocab.eos_id)
 
 
-@pytest.mark.parametrize("dtype,steps", [(torch.bfloat16, 48), (torch.float32, 16),
+@pytest.mark.parametrize("dtype,steps", [(torch.bfloat16, 64), (torch.float32, 16),
                                          (torch.float16, 16)])
 def test_device_loop_matches_oracle(dtype: torch.dtype, steps: int) -> None:
     """The device-turnover loop: before every step the row lists and counts
