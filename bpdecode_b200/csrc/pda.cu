@@ -974,12 +974,13 @@ __device__ __forceinline__ const uint32_t* row_bits(const Memo& memo, const Work
 }
 
 // Row -> its allow words through the memo / workspace (nullptr for broken rows).
-// In place, PDA rows are mostly rejected tiles that go out as bulk fills: a
-// CTA takes twice the dense chunk (8 warp tiles a warp), so fewer CTAs per
-// row meet in the argmax merge (config 4, 256 rows: 39.0 against 40.1-40.8 us
-// per step from a graph, same box; the miss-path workloads unchanged). The
-// step from the model's rows keeps the dense chunk (config-5 serving step
-// 147.8 against 148.4-148.6 us with the larger one).
+// PDA rows are mostly rejected tiles (bulk fills in place, nothing read from
+// the model's rows): a CTA takes twice the dense chunk (8 warp tiles a warp),
+// so fewer CTAs per row meet in the argmax merge and fewer blocks of a step
+// over a device-held row count find no row. Config 4 (256 rows, in place):
+// 39.0 against 40.1-40.8 us per step from a graph, the miss-path workloads
+// unchanged; the config-5 serving step, whose PDA rows run beside the dense
+// rows' step: 127.4 against 133.5 us (same box).
 #ifndef BPD_PDA_TILES_PER_WARP
 #define BPD_PDA_TILES_PER_WARP 8
 #endif

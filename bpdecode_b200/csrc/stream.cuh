@@ -884,8 +884,7 @@ bpd_status launch_stream_step_src(const void* src, int64_t src_stride, const int
   if (scratch == nullptr) return fail(BPD_ERR_INVALID, "%s: null step scratch", what);
   if (!aligned16(scratch))
     return fail(BPD_ERR_INVALID, "%s: step scratch not 16-byte aligned", what);
-  // every Rows type takes the dense chunk here (measured best for PDA rows too)
-  const int32_t chunk = stream_chunk<float>(V, chunks_per_row, batch);
+  const int32_t chunk = stream_chunk<float>(V, chunks_per_row, batch, Rows::kTilesPerWarp);
   const int32_t cpr = (V + chunk - 1) / chunk;
   const int64_t grid = static_cast<int64_t>(batch) * cpr;
   if (grid >= 0x7FFFFFFF) return fail(BPD_ERR_INVALID, "%s: batch too large", what);
