@@ -397,7 +397,9 @@ def run_config5(args: argparse.Namespace) -> None:
                    "l2": f"{ring} logits buffers of 262 MB cycled (larger than L2)",
                    "table_build_s": build_s},
         "clocks": clocks.summary(),
-        "gpu_launches": steps * 6,
+        # per step: the dense soft step; prologue, lookup, compute and the
+        # PDA step (second stream); the token gather; the turnover
+        "gpu_launches": steps * 7,
         "timing": "CUDA events around the graph replays (a step = dense soft step, PDA "
                   "mask pipeline + step, token gather, device turnover); max over ranks",
         "host_turnover_loop": {"ms_per_step": host_ms,
