@@ -608,8 +608,8 @@ struct DenseCommit {
 #endif
 
 // Chunk of one CTA: `chunks_per_row` CTAs per row when the caller asks for
-// it, else BPD_TILES_PER_WARP warp tiles per warp. Always a multiple of
-// kWarps warp tiles, so every warp span starts on a tile.
+// it, else `tiles_per_warp` warp tiles per warp (the Rows type's count).
+// Always a multiple of kWarps warp tiles, so every warp span starts on a tile.
 //
 // With `batch` given, small batches are cut finer (down to one warp tile per
 // warp) until the grid has about one CTA per SM, so a step over a handful of

@@ -192,6 +192,32 @@ def test_device_loop_graph_replay_equals_eager() -> None:
     del graphs
 
 
+def test_device_loop_second_stream_equals_one_stream() -> None:
+    """The PDA rows' launches on a second stream (the default) make the same
+    decisions as the whole step on one stream: tokens, states, config rows,
+    broken flags and the mix, step after step with turnover."""
+    from bpdecode_b200.serving import DeviceServingLoop
+    from bpdecode_b200.workloads import DENSE_PATTERNS
+
+    dense, pda, vocab = _grammars(4096)
+    rows = 96
+    one, two = (DeviceServingLoop(rows, dense, pda, n_regex=len(DENSE_PATTERNS), seed=9,
+                                  overlap=ov) for ov in (False, True))
+    assert one._side is None and two._side is not None
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    for step in range(16):
+        logits = (torch.randn(rows, vocab.size, generator=gen, device="cuda") * 2).to(
+            torch.bfloat16)
+        ta = one.step(logits).clone()
+        one.turnover()
+        tb = two.step(logits).clone()
+        two.turnover()
+        assert torch.equal(ta, tb), step
+        for x, y in zip(one.states(), two.states()):
+            assert torch.equal(x, y), step
+        assert torch.equal(one.kind, two.kind), step
+
+
 def test_device_turnover_lists_over_many_rows() -> None:
     """The device turnover over 2500 rows (three blocks of the kernel's
     1024-row compaction): after every call the ascending row lists and their
