@@ -187,8 +187,12 @@ __device__ __forceinline__ uint64_t l2_evict_last_policy() {
   return policy;
 }
 
-// Warp tiles whose allow words a warp loads at once.
-constexpr int kGroupTiles = 4;
+// Warp tiles whose allow words a warp loads at once (8, with the L2 warm-up,
+// spilled registers: config-2 step 97-99 against 82-84 us).
+#ifndef BPD_GROUP_TILES
+#define BPD_GROUP_TILES 4
+#endif
+constexpr int kGroupTiles = BPD_GROUP_TILES;
 
 // Cache policy of the logits stream: 0 = streaming (evict-first) loads and
 // stores, 1 = loads and stores cached at L2 only (.cg). .cg measured 2 %
@@ -263,6 +267,32 @@ __device__ __forceinline__ uint32_t tile_bits(uint32_t w, int32_t lane, int j) {
 #define BPD_PIPELINE 1
 #endif
 
+// L2 warm-up of a group's later live tiles, issued as soon as the group's
+// allow words are known, so their DRAM reads overlap the first live tile
+// instead of starting one tile after another: 0 = off, 1 = per lane, the
+// vectors the tile loop will load (prefetch.global.L2), 2 = the whole tile in
+// one bulk prefetch by one lane (cp.async.bulk.prefetch.L2), 3 = mode 1 for
+// in-place spans and mode 2 for spans that read another buffer. Same-box A/B
+// against 0: mode 3 takes the config-2 fused step from 87.9 to 82.8 us over
+// the first 20 steps of a generation (62.4 -> 61.4 over 128), the tokens-only
+// step from 63.0 to 58.9 us, the config-3 fp32 step from 74.3 to 71.0 us; the
+// PDA config-4 step, the soft step and config 5 are unchanged. Mode 1 alone
+// made the tokens-only step 2 % slower, mode 2 alone the fused step 1 %
+// slower than mode 3 (bulk prefetches also fetch the rejected vectors that
+// the in-place step writes without reading).
+#ifndef BPD_L2_PREFETCH
+#define BPD_L2_PREFETCH 3
+#endif
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // One warp masks [e0, e1) of `row` (e0 a multiple of the warp tile, so allow
 // words line up) against allow row `brow` (nullptr = reject everything); no
 // barrier, no shared state with the CTA's other warps except the read-only
@@ -312,6 +342,10 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
   constexpr int WPT = TILE / 32;  // allow words per warp tile
   constexpr uint32_t FULL = (1u << EPV) - 1u;
   const int32_t lane = threadIdx.x & 31;
+  // L2 warm-up mode of this span (BPD_L2_PREFETCH 3: per lane in place,
+  // whole tiles when the values come from another buffer)
+  constexpr int kPrefetch =
+      BPD_L2_PREFETCH == 3 ? (kInPlace ? 1 : 2) : BPD_L2_PREFETCH;
   int32_t fill_first = INT_MAX;  // lowest index this lane wrote `fill` to
   VecArg va;
   if constexpr (kVec) {
@@ -328,6 +362,27 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
 #pragma unroll
       for (int t = 0; t < kGroupTiles; ++t)
         live |= (__any_sync(kAll, w[t] != 0u) ? 1u : 0u) << t;
+      if constexpr (!kSoft && BPD_PIPELINE && kPrefetch != 0) {
+        // every live tile after the first: the first is loaded right away
+        const uint32_t later = live & (live - 1u);
+        if constexpr (kPrefetch == 1) {
+#pragma unroll
+          for (int t = 1; t < kGroupTiles; ++t) {
+            if (((later >> t) & 1u) == 0u) continue;
+            const int32_t tb = e0 + (g0 + t) * TILE;
+#pragma unroll
+            for (int j = 0; j < kVPT; ++j) {
+              const uint32_t b = tile_bits<T>(w[t], lane, j);
+              const bool need = (kArgmax || !kInPlace) ? (b != 0u) : (b != 0u && b != FULL);
+              if (need) prefetch_l2(srow + tb + (lane + 32 * j) * EPV);
+            }
+          }
+        } else {
+          if (lane < kGroupTiles && ((later >> lane) & 1u) != 0u)
+            bulk_prefetch_l2(srow + e0 + (g0 + lane) * TILE,
+                             static_cast<uint32_t>(TILE * static_cast<int32_t>(sizeof(S))));
+        }
+      }
       const int32_t ng = min(kGroupTiles, ntiles - g0);
       uint32_t dead = ((1u << ng) - 1u) & ~live;
       if constexpr (sizeof(Bits) == 4) {
