@@ -288,6 +288,23 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+// The same with evict-last priority (the soft step's lookahead rows, which
+// rows in the same state share).
+__device__ __forceinline__ void prefetch_l2_keep(const void* p) {
+  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+
+// Soft spans: 0 = no L2 warm-up, 1 = per lane (logits and biases of every
+// vector with an allowed token), 2 = whole tiles by one lane per tile, 3 =
+// mode 1 for in-place spans, none for spans that read another buffer.
+// Same-box A/B against 0: mode 1 takes the in-place fp32 soft step (1024
+// rows) from 122.2 to 118.6 us but the config-5 loop, whose soft step reads
+// bf16 model logits into an fp32 result, from 127.4 to 137.3 us; mode 2 is
+// slower on both (124.3, 129.2).
+#ifndef BPD_SOFT_PREFETCH
+#define BPD_SOFT_PREFETCH 3
+#endif
+
 // p 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -362,6 +379,33 @@ __device__ __forceinline__ void warp_span(T* __restrict__ row, const S* __restri
 #pragma unroll
       for (int t = 0; t < kGroupTiles; ++t)
         live |= (__any_sync(kAll, w[t] != 0u) ? 1u : 0u) << t;
+      constexpr int kSoftPrefetch =
+          BPD_SOFT_PREFETCH == 3 ? (kInPlace ? 1 : 0) : BPD_SOFT_PREFETCH;
+      if constexpr (kSoft && kSoftPrefetch != 0) {
+        // soft spans load a tile's vectors a group at a time, so every live
+        // tile is warmed, logits and lookahead biases alike
+        if constexpr (kSoftPrefetch == 1) {
+#pragma unroll
+          for (int t = 0; t < kGroupTiles; ++t) {
+            if (((live >> t) & 1u) == 0u) continue;
+            const int32_t tb = e0 + (g0 + t) * TILE;
+#pragma unroll
+            for (int j = 0; j < kVPT; ++j) {
+              if (tile_bits<T>(w[t], lane, j) == 0u) continue;
+              const int32_t e = tb + (lane + 32 * j) * EPV;
+              prefetch_l2(srow + e);
+              prefetch_l2_keep(lrow + e);
+            }
+          }
+        } else {
+          if (lane < kGroupTiles && ((live >> lane) & 1u) != 0u) {
+            const int32_t tb = e0 + (g0 + lane) * TILE;
+            bulk_prefetch_l2(srow + tb,
+                             static_cast<uint32_t>(TILE * static_cast<int32_t>(sizeof(S))));
+            bulk_prefetch_l2(lrow + tb, static_cast<uint32_t>(TILE * 4));
+          }
+        }
+      }
       if constexpr (!kSoft && BPD_PIPELINE && kPrefetch != 0) {
         // every live tile after the first: the first is loaded right away
         const uint32_t later = live & (live - 1u);
